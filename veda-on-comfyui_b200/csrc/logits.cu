@@ -1,0 +1,147 @@
+// Kernel (1b): Veda predictor tile logits (core/predictor.py:63-80):
+//   x_hat = F @ P[h] + F[:, :128]      (F = [mean | max | min], 384 wide)
+//   logits[h, i, j] = q_hat_i . k_hat_j / sqrt(128)
+// fp32 on CUDA cores: about 1.2 GFLOP for 24 heads x 256 tiles, far below
+// anything worth a tensor-core pipeline, and fp32 keeps the logits (and so
+// the selection) within rounding of the reference's fp32 bmm.
+#include "common.cuh"
+
+namespace veda {
+namespace {
+
+constexpr int kFeat = 3 * kDim;   // 384
+constexpr int kProjRows = 16;     // rows of F per CTA in the projection
+constexpr int kLogitTile = 32;    // 32 x 32 logits per CTA
+
+template <typename PT>
+__device__ __forceinline__ float to_f(PT v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) {
+  return __half2float(v);
+}
+
+// grid (ceil(n / 16), heads, 2): z = 0 projects q features, z = 1 k.
+template <typename PT>
+__global__ void __launch_bounds__(256)
+    project_kernel(const float* fq, const float* fk, const PT* pq,
+                   const PT* pk, int n_q, int n_k, float* hat_q,
+                   float* hat_k) {
+  __shared__ float f_sh[kProjRows][kFeat];
+  const bool is_k = blockIdx.z == 1;
+  const int n = is_k ? n_k : n_q;
+  const int head = blockIdx.y;
+  const int row0 = blockIdx.x * kProjRows;
+  if (row0 >= n) return;
+  const float* f = (is_k ? fk : fq) + (static_cast<int64_t>(head) * n + row0) * kFeat;
+  const PT* proj = (is_k ? pk : pq) + static_cast<int64_t>(head) * kFeat * kDim;
+  float* out = (is_k ? hat_k : hat_q) + (static_cast<int64_t>(head) * n + row0) * kDim;
+  const int rows = min(kProjRows, n - row0);
+  for (int i = threadIdx.x; i < kProjRows * kFeat; i += blockDim.x) {
+    const int r = i / kFeat;
+    f_sh[r][i % kFeat] = r < rows ? f[i] : 0.0f;
+  }
+  __syncthreads();
+  const int d = threadIdx.x & (kDim - 1);
+  const int r0 = (threadIdx.x >> 7) * (kProjRows / 2);
+  float acc[kProjRows / 2];
+#pragma unroll
+  for (int r = 0; r < kProjRows / 2; ++r) acc[r] = 0.0f;
+  for (int k = 0; k < kFeat; ++k) {
+    const float w = to_f(proj[static_cast<int64_t>(k) * kDim + d]);
+#pragma unroll
+    for (int r = 0; r < kProjRows / 2; ++r)
+      acc[r] = fmaf(f_sh[r0 + r][k], w, acc[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < kProjRows / 2; ++r)
+    if (r0 + r < rows) out[(r0 + r) * kDim + d] = acc[r] + f_sh[r0 + r][d];
+}
+
+// grid (ceil(n_k / 32), ceil(n_q / 32), heads), 256 threads, 4 logits each.
+__global__ void __launch_bounds__(256)
+    logits_kernel(const float* hat_q, const float* hat_k, int n_q, int n_k,
+                  float* logits) {
+  __shared__ float q_sh[kLogitTile][kDim + 1];
+  __shared__ float k_sh[kLogitTile][kDim + 1];
+  const int head = blockIdx.z;
+  const int i0 = blockIdx.y * kLogitTile, j0 = blockIdx.x * kLogitTile;
+  const float* qh = hat_q + static_cast<int64_t>(head) * n_q * kDim;
+  const float* kh = hat_k + static_cast<int64_t>(head) * n_k * kDim;
+  for (int e = threadIdx.x; e < kLogitTile * kDim; e += blockDim.x) {
+    const int r = e / kDim, c = e % kDim;
+    q_sh[r][c] = i0 + r < n_q ? qh[static_cast<int64_t>(i0 + r) * kDim + c] : 0.0f;
+    k_sh[r][c] = j0 + r < n_k ? kh[static_cast<int64_t>(j0 + r) * kDim + c] : 0.0f;
+  }
+  __syncthreads();
+  const int tj = threadIdx.x & 31;
+  const int ti = (threadIdx.x >> 5) * 4;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int c = 0; c < kDim; ++c) {
+    const float kv = k_sh[tj][c];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[r] = fmaf(q_sh[ti + r][c], kv, acc[r]);
+  }
+  const float root = 11.313708498984761f;  // sqrt(128)
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = i0 + ti + r, j = j0 + tj;
+    if (i < n_q && j < n_k)
+      logits[(static_cast<int64_t>(head) * n_q + i) * n_k + j] =
+          __fdiv_rn(acc[r], root);
+  }
+}
+
+}  // namespace
+}  // namespace veda
+
+using namespace veda;
+
+extern "C" int veda_tile_logits(const float* feats_q, const float* feats_k,
+                                const void* proj_q, const void* proj_k,
+                                int proj_dtype, int heads, int n_q, int n_k,
+                                float* workspace, float* logits,
+                                void* stream) {
+  if (int rc = check_device()) return rc;
+  if (heads <= 0 || heads > 65535 || n_q <= 0 || n_k <= 0)
+    return fail(VEDA_ERR_INVALID, "bad sizes: heads %d, n_q %d, n_k %d", heads,
+                n_q, n_k);
+  if (feats_q == nullptr || feats_k == nullptr || proj_q == nullptr ||
+      proj_k == nullptr || workspace == nullptr || logits == nullptr)
+    return fail(VEDA_ERR_INVALID, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* hat_q = workspace;
+  float* hat_k = workspace + static_cast<int64_t>(heads) * n_q * kDim;
+  const int n_max = n_q > n_k ? n_q : n_k;
+  dim3 pgrid((n_max + kProjRows - 1) / kProjRows, heads, 2);
+  switch (proj_dtype) {
+    case VEDA_BF16:
+      project_kernel<__nv_bfloat16><<<pgrid, 256, 0, s>>>(
+          feats_q, feats_k, static_cast<const __nv_bfloat16*>(proj_q),
+          static_cast<const __nv_bfloat16*>(proj_k), n_q, n_k, hat_q, hat_k);
+      break;
+    case VEDA_F16:
+      project_kernel<__half><<<pgrid, 256, 0, s>>>(
+          feats_q, feats_k, static_cast<const __half*>(proj_q),
+          static_cast<const __half*>(proj_k), n_q, n_k, hat_q, hat_k);
+      break;
+    case VEDA_F32:
+      project_kernel<float><<<pgrid, 256, 0, s>>>(
+          feats_q, feats_k, static_cast<const float*>(proj_q),
+          static_cast<const float*>(proj_k), n_q, n_k, hat_q, hat_k);
+      break;
+    default:
+      return fail(VEDA_ERR_INVALID, "proj dtype must be bf16, fp16 or fp32");
+  }
+  VEDA_CHECK_CUDA(cudaGetLastError());
+  dim3 lgrid((n_k + kLogitTile - 1) / kLogitTile,
+             (n_q + kLogitTile - 1) / kLogitTile, heads);
+  logits_kernel<<<lgrid, 256, 0, s>>>(hat_q, hat_k, n_q, n_k, logits);
+  VEDA_CHECK_CUDA(cudaGetLastError());
+  return VEDA_OK;
+}

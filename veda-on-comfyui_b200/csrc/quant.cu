@@ -1,0 +1,288 @@
+// Kernel (2): per-block INT8 quantisation of Q and K, fused with the
+// TripPool features of kernel (1), in one read of each 128-row tile.
+//
+// Arithmetic of kernels/sage/sparse_int8.py:57-73 (reference): x * pre_scale
+// in fp32; scale = max|x| / 127 per (block, head), 1 for an all-zero block;
+// q = x / scale; q += 0.5 * sign (>= 0 counts as positive); int8 = trunc(q).
+// IEEE-rounded division (__fdiv_rn), so the int8 codes are bit-exact with an
+// fp32 restatement of those steps.
+//
+// Pooling follows core/predictor.py:20-60: mean (fp32 sum / max(valid, 1)),
+// max and min over the real rows of each video tile, all 0 for an empty tile.
+//
+// One CTA of 256 threads per (tile, head, tensor); thread t loads 8 rows x 8
+// dims with 16-byte vector loads (16 threads cover one 256-byte row).
+#include "common.cuh"
+
+namespace veda {
+namespace {
+
+constexpr int kQuantThreads = 256;
+
+struct QuantJob {
+  const void* x;     // [n_slots, heads, 128] 16-bit
+  int8_t* out;       // [heads][n_slots][128]
+  float* scale;      // [heads][n_slots / block]
+  float* feats;      // [heads][n_video][384] or null
+  float pre_scale;
+  int block;         // 64 or 128
+};
+
+struct QuantParams {
+  QuantJob job[2];
+  int64_t stride_n, stride_h;  // elements
+  int n_tiles;
+  const int32_t* valid;        // [n_tiles] or null (all 128)
+  int n_video;
+};
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* f) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ void load8(const __half* p, float* f) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
+}
+
+__device__ __forceinline__ int8_t quant_one(float x, float scale) {
+  float q = __fdiv_rn(x, scale);
+  q = __fadd_rn(q, q >= 0.0f ? 0.5f : -0.5f);
+  return static_cast<int8_t>(__float2int_rz(q));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kQuantThreads)
+    quant_pool_kernel(const QuantParams p) {
+  __shared__ float amax_sh[8][2];
+  __shared__ float pool_sh[8][3][kDim];
+  __shared__ float scale_sh[2];
+
+  const QuantJob job = blockIdx.z == 0 ? p.job[0] : p.job[1];
+  const int tile = blockIdx.x, head = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int dc = tid & 15;  // dims 8*dc .. 8*dc+7
+  const int rg = tid >> 4;  // rows rg + 16 i
+  const int valid = p.valid != nullptr ? __ldg(p.valid + tile) : kTile;
+
+  const T* x = static_cast<const T*>(job.x) +
+               static_cast<int64_t>(tile) * kTile * p.stride_n +
+               static_cast<int64_t>(head) * p.stride_h + 8 * dc;
+  float v[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) load8(x + (rg + 16 * i) * p.stride_n, v[i]);
+
+  // TripPool over the real rows (a prefix of the tile), before pre-scaling.
+  const bool pool = job.feats != nullptr && tile < p.n_video;
+  if (pool) {
+    float s[8], mx[8], mn[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      s[e] = 0.0f;
+      mx[e] = -INFINITY;
+      mn[e] = INFINITY;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (rg + 16 * i < valid) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          s[e] += v[i][e];
+          mx[e] = fmaxf(mx[e], v[i][e]);
+          mn[e] = fminf(mn[e], v[i][e]);
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      s[e] += __shfl_xor_sync(0xffffffffu, s[e], 16);
+      mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
+      mn[e] = fminf(mn[e], __shfl_xor_sync(0xffffffffu, mn[e], 16));
+    }
+    if (lane < 16) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        pool_sh[warp][0][8 * dc + e] = s[e];
+        pool_sh[warp][1][8 * dc + e] = mx[e];
+        pool_sh[warp][2][8 * dc + e] = mn[e];
+      }
+    }
+  }
+
+  if (job.pre_scale != 1.0f) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = __fmul_rn(v[i][e], job.pre_scale);
+  }
+
+  // max |x| of rows 0-63 (a[0]) and 64-127 (a[1]).
+  float a[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a[i >> 2] = fmaxf(a[i >> 2], fabsf(v[i][e]));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    a[0] = fmaxf(a[0], __shfl_xor_sync(0xffffffffu, a[0], off));
+    a[1] = fmaxf(a[1], __shfl_xor_sync(0xffffffffu, a[1], off));
+  }
+  if (lane == 0) {
+    amax_sh[warp][0] = a[0];
+    amax_sh[warp][1] = a[1];
+  }
+  __syncthreads();
+  if (tid < 2) {
+    float m0 = 0.0f, m1 = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      m0 = fmaxf(m0, amax_sh[w][0]);
+      m1 = fmaxf(m1, amax_sh[w][1]);
+    }
+    float m = tid == 0 ? m0 : m1;
+    if (job.block == kTile) m = fmaxf(m0, m1);
+    float sc = __fdiv_rn(m, 127.0f);
+    scale_sh[tid] = sc > 0.0f ? sc : 1.0f;
+  }
+  if (pool && tid < kDim) {
+    float s = 0.0f, mx = -INFINITY, mn = INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      s += pool_sh[w][0][tid];
+      mx = fmaxf(mx, pool_sh[w][1][tid]);
+      mn = fminf(mn, pool_sh[w][2][tid]);
+    }
+    float* f = job.feats + (static_cast<int64_t>(head) * p.n_video + tile) * 3 * kDim;
+    const bool live = valid > 0;
+    f[tid] = live ? __fdiv_rn(s, static_cast<float>(valid)) : 0.0f;
+    f[kDim + tid] = live ? mx : 0.0f;
+    f[2 * kDim + tid] = live ? mn : 0.0f;
+  }
+  __syncthreads();
+
+  const float sc[2] = {scale_sh[0], scale_sh[1]};
+  const int64_t n_slots = static_cast<int64_t>(p.n_tiles) * kTile;
+  int8_t* out = job.out + (static_cast<int64_t>(head) * n_slots +
+                           static_cast<int64_t>(tile) * kTile) * kDim + 8 * dc;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float s = sc[i >> 2];
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      lo |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one(v[i][e], s))) << (8 * e);
+      hi |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one(v[i][e + 4], s))) << (8 * e);
+    }
+    *reinterpret_cast<uint2*>(out + (rg + 16 * i) * kDim) = make_uint2(lo, hi);
+  }
+  if (tid == 0) {
+    if (job.block == kTile) {
+      job.scale[static_cast<int64_t>(head) * p.n_tiles + tile] = sc[0];
+    } else {
+      float* s = job.scale + static_cast<int64_t>(head) * 2 * p.n_tiles + 2 * tile;
+      s[0] = sc[0];
+      s[1] = sc[1];
+    }
+  }
+}
+
+int launch_quant(const QuantParams& p, int n_jobs, int heads, int dtype,
+                 cudaStream_t stream) {
+  dim3 grid(p.n_tiles, heads, n_jobs);
+  if (dtype == VEDA_BF16)
+    quant_pool_kernel<__nv_bfloat16><<<grid, kQuantThreads, 0, stream>>>(p);
+  else
+    quant_pool_kernel<__half><<<grid, kQuantThreads, 0, stream>>>(p);
+  VEDA_CHECK_CUDA(cudaGetLastError());
+  return VEDA_OK;
+}
+
+int check_input(const void* x, int dtype, int64_t stride_n, int64_t stride_h,
+                int n_slots, int heads) {
+  if (x == nullptr) return fail(VEDA_ERR_INVALID, "null input");
+  if (dtype != VEDA_BF16 && dtype != VEDA_F16)
+    return fail(VEDA_ERR_INVALID, "input dtype must be bf16 or fp16");
+  if (n_slots <= 0 || n_slots % kTile != 0 || heads <= 0)
+    return fail(VEDA_ERR_INVALID,
+                "n_slots (%d) must be a positive multiple of 128, heads (%d) "
+                "positive", n_slots, heads);
+  if (n_slots / kTile > 65535 || heads > 65535)
+    return fail(VEDA_ERR_INVALID, "too many tiles or heads for one launch");
+  if (!aligned16(x) || (stride_n * 2) % 16 != 0 || (stride_h * 2) % 16 != 0)
+    return fail(VEDA_ERR_INVALID,
+                "input rows must be 16-byte aligned (base, row and head "
+                "strides)");
+  return VEDA_OK;
+}
+
+}  // namespace
+}  // namespace veda
+
+using namespace veda;
+
+extern "C" int veda_quantize(const void* x, int dtype, int64_t stride_n,
+                             int64_t stride_h, int n_slots, int heads, int dim,
+                             int block, float pre_scale, int8_t* out,
+                             float* scale, void* stream) {
+  if (int rc = check_device()) return rc;
+  if (dim != kDim) return fail(VEDA_ERR_INVALID, "head dim must be 128");
+  if (block != 64 && block != 128)
+    return fail(VEDA_ERR_INVALID, "block must be 64 or 128");
+  if (int rc = check_input(x, dtype, stride_n, stride_h, n_slots, heads))
+    return rc;
+  if (out == nullptr || scale == nullptr || !aligned16(out))
+    return fail(VEDA_ERR_INVALID, "null or misaligned output");
+  QuantParams p{};
+  p.job[0] = QuantJob{x, out, scale, nullptr, pre_scale, block};
+  p.stride_n = stride_n;
+  p.stride_h = stride_h;
+  p.n_tiles = n_slots / kTile;
+  p.valid = nullptr;
+  p.n_video = 0;
+  return launch_quant(p, 1, heads, dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int veda_quant_pool(const void* q, const void* k, int dtype,
+                               int64_t stride_n, int64_t stride_h, int n_slots,
+                               int heads, const int32_t* valid_count,
+                               int n_video_tiles, float q_pre_scale,
+                               int8_t* q_i8, float* q_scale, int8_t* k_i8,
+                               float* k_scale, float* feats_q, float* feats_k,
+                               void* stream) {
+  if (int rc = check_device()) return rc;
+  if (int rc = check_input(q, dtype, stride_n, stride_h, n_slots, heads))
+    return rc;
+  if (int rc = check_input(k, dtype, stride_n, stride_h, n_slots, heads))
+    return rc;
+  if (q_i8 == nullptr || k_i8 == nullptr || q_scale == nullptr ||
+      k_scale == nullptr || !aligned16(q_i8) || !aligned16(k_i8))
+    return fail(VEDA_ERR_INVALID, "null or misaligned output");
+  const int n_tiles = n_slots / kTile;
+  if ((feats_q != nullptr) != (feats_k != nullptr))
+    return fail(VEDA_ERR_INVALID, "feats_q and feats_k go together");
+  if (feats_q != nullptr &&
+      (valid_count == nullptr || n_video_tiles < 0 || n_video_tiles > n_tiles))
+    return fail(VEDA_ERR_INVALID,
+                "pooling needs valid_count and 0 <= n_video_tiles <= n_tiles");
+  QuantParams p{};
+  p.job[0] = QuantJob{q, q_i8, q_scale, feats_q, q_pre_scale, kTile};
+  p.job[1] = QuantJob{k, k_i8, k_scale, feats_k, 1.0f, kKeyBlock};
+  p.stride_n = stride_n;
+  p.stride_h = stride_h;
+  p.n_tiles = n_tiles;
+  p.valid = valid_count;
+  p.n_video = feats_q != nullptr ? n_video_tiles : 0;
+  return launch_quant(p, 2, heads, dtype, static_cast<cudaStream_t>(stream));
+}
