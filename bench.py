@@ -1,0 +1,453 @@
+"""Benchmark of the Veda sparse-attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: one generated-video attention layer, B=1,
+H=24, head_dim 128, L=32,760 real tokens padded to 32,768 (256 tiles of
+128), Q/K/V bf16 ~N(0,1) with a per-(head, channel) K offset ~N(0, 2^2),
+tile scores ~U(0,1), 26 of 256 key tiles kept per query tile (90% sparse),
+INT8 QK^T with fp32 scales and 16-bit PV.
+
+A step is one Veda attention call: top-k selection into index lists, the
+fused Q/K INT8 quantisation, the tcgen05 block-sparse attention kernel, and
+at N > 1 the NCCL all-gather of the head-sharded output (heads split
+contiguously over the ranks). Inputs are resident in HBM; steps rotate over
+input sets whose total exceeds L2 (126 MB) several times, so no step reads
+another's data from L2. The metric is effective TFLOPS: the algorithmic
+work of the tiles actually evaluated (2*128^3 INT8 ops for QK^T plus
+2*128^3 16-bit FLOPs for PV per kept tile pair) divided by the call's
+latency (max over ranks); `ms_per_step` is that latency.
+
+`e2e` repeats the call through the same API with the inputs copied in from
+pinned host memory and the output copied back inside the timed region.
+`--impl reference` times the reference's CPU path for this layer (its
+selection and its fp32 masked attention, restated in numpy under oracle/)
+on the host cores, on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, 'veda-on-comfyui_b200'))
+sys.path.insert(0, HERE)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = ('sparse-attn call latency (ms) & effective TFLOPS at L=32k, 90% '
+          'sparse, 1/2/4/8 B200')
+HEADS, DIM, SEQ, REAL, KEEP = 24, 128, 32768, 32760, 26
+N_TILES = SEQ // 128
+OPS_PER_PAIR = 2 * 128 ** 3 * 2          # INT8 QK^T + 16-bit PV
+L2_BYTES = 126 * 2 ** 20
+WORKLOAD = ('cfg1: B=1 H=24 D=128 L=32760 padded to 32768 (256 tiles), '
+            '26 of 256 key tiles per query tile (90% sparse), bf16 in, '
+            'INT8 QK^T + bf16 PV')
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__.split('\n')[0])
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=100)
+    p.add_argument('--warmup', type=int, default=5)
+    p.add_argument('--impl', choices=['ours', 'reference'], default='ours')
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    return p.parse_args()
+
+
+# --------------------------------------------------------------- helpers
+
+def measured_peaks() -> dict:
+    path = os.path.join(HERE, 'MEASURED_PEAKS.json')
+    if os.path.exists(path):
+        with open(path) as f:
+            peaks = json.load(f)
+        return {'hbm_gbs': peaks['hbm_gbs'], 'bf16_tflops': peaks['bf16_tflops'],
+                'source': 'measured (MEASURED_PEAKS.json)'}
+    return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0, 'source': 'fallback'}
+
+
+def measure_int8_peak(device) -> float:
+    """Dense INT8 tensor-core throughput of cuBLAS (torch._int_mm 8192^3),
+    best of 10, in TOPS."""
+    n = 8192
+    a = torch.randint(-127, 127, (n, n), dtype=torch.int8, device=device)
+    b = torch.randint(-127, 127, (n, n), dtype=torch.int8, device=device).t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = float('inf')
+    for _ in range(10):
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        torch._int_mm(a, b)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def profile_traffic() -> float | None:
+    """DRAM bytes per attention launch from the committed ncu summary."""
+    path = os.path.join(HERE, 'profiles', 'sparse_attention_cfg1.md')
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        m = re.search(r'traffic_bytes_per_launch:\s*([0-9.eE+]+)', f.read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms."""
+
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,'
+              'clocks_event_reasons.hw_slowdown,'
+              'clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,'
+              'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', f'--id={self.index}',
+                 f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                 '-lms', '50'], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown',
+                 'sw_power_cap']
+        for line in getattr(self, 'lines', []):
+            parts = [p.strip() for p in line.split(',')]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[4:8]):
+                if flag.lower() == 'active':
+                    reasons.add(name)
+        loaded = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {'sm_mhz': statistics.median(loaded) if loaded else None,
+                'sm_max_mhz': mx, 'samples': len(sm),
+                'reasons': sorted(reasons)}
+
+
+# ------------------------------------------------------------ workload
+
+def make_set(set_id: int, heads: range, device) -> dict:
+    """One input set for the given heads: q/k/v [SEQ, h, 128] bf16 (rows
+    past REAL are padding, zero), scores [h, 256, 256] fp32."""
+    qs, ks, vs, ss = [], [], [], []
+    for h in heads:
+        g = torch.Generator(device=device)
+        g.manual_seed(1_000_003 * set_id + 7919 * h + 11)
+        q, k, v = (torch.randn(SEQ, DIM, generator=g, device=device)
+                   for _ in range(3))
+        k = k + torch.randn(DIM, generator=g, device=device) * 2.0
+        for t in (q, k, v):
+            t[REAL:] = 0
+        qs.append(q)
+        ks.append(k)
+        vs.append(v)
+        ss.append(torch.rand(N_TILES, N_TILES, generator=g, device=device))
+    stack = lambda ts: torch.stack(ts, 1).to(torch.bfloat16).contiguous()
+    return {'q': stack(qs), 'k': stack(ks), 'v': stack(vs),
+            'scores': torch.stack(ss, 0).contiguous()}
+
+
+class Call:
+    """One Veda attention call on this rank's heads (the timed step)."""
+
+    def __init__(self, n_local: int, device, group=None, world=1):
+        from veda_b200 import kernels, selection, tiling
+        self.kernels = kernels
+        self.layout = tiling.identity_layout(REAL, device)
+        self.blocks = selection.column_blocks(
+            self.layout, selection.Budget(tiles=KEEP),
+            selection.Budget(ratio=1.0))
+        self.spec, self.extra = selection.kernel_blocks(
+            self.layout, self.blocks, device)
+        self.width = selection.list_width(self.layout, self.blocks)
+        self.device = device
+        self.group, self.world = group, world
+        self.quant = {}
+        self.out = torch.empty(SEQ, n_local, DIM, dtype=torch.bfloat16,
+                               device=device)
+        self.gathered = torch.empty(world, SEQ, n_local, DIM,
+                                    dtype=torch.bfloat16, device=device) \
+            if world > 1 else None
+        self.pre = DIM ** -0.5 * kernels.LOG2E
+
+    def __call__(self, s: dict, events=None):
+        from veda_b200 import ops
+        rec = (lambda i: events[i].record()) if events else (lambda i: None)
+        rec(0)
+        index, count = ops.select_index(s['scores'], self.layout.kv_ok,
+                                        N_TILES, self.spec, self.extra,
+                                        self.width)
+        rec(1)
+        quant = ops.quant_pool(s['q'], s['k'], self.layout.valid_count, 0,
+                               self.pre, pool=False, out=self.quant)
+        rec(2)
+        ops.sparse_attention(quant['q_i8'], quant['q_scale'], quant['k_i8'],
+                             quant['k_scale'], s['v'], index, count,
+                             self.layout.valid_count, out=self.out)
+        rec(3)
+        if self.gathered is not None:
+            torch.distributed.all_gather_into_tensor(self.gathered, self.out,
+                                                     group=self.group)
+        rec(4)
+        return count
+
+
+def cpu_reference(seconds_hint: float = 15.0) -> dict:
+    """The reference's CPU path for one head of the workload (selection +
+    fp32 masked attention, oracle/ numpy restatement), timed on the host."""
+    from oracle import attention as oatt
+    from oracle import selection as osel
+    from oracle import tiling as otil
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(2024)
+    q, k, v = (torch.randn(SEQ, DIM, generator=g) for _ in range(3))
+    k = k + torch.randn(DIM, generator=g) * 2.0
+    q, k, v = (t.to(torch.bfloat16).float().numpy() for t in (q, k, v))
+    q[REAL:] = k[REAL:] = v[REAL:] = 0
+    scores = torch.rand(1, N_TILES, N_TILES, generator=g).numpy()
+    layout = otil.identity_layout(REAL)
+    t0 = time.perf_counter()
+    blocks = osel.column_blocks(layout, osel.Budget(tiles=KEEP),
+                                osel.Budget(ratio=1.0))
+    index, count = osel.index_lists(scores, layout, blocks)
+    mask = oatt.mask_from_lists(index, count, layout.n_tiles)[0]
+    rows_done, pairs = 0, 0
+    chunk = 2048
+    while rows_done < SEQ:
+        rows = np.arange(rows_done, rows_done + chunk)
+        oatt.block_sparse_head(q, k, v, mask, layout.slot_valid, rows=rows)
+        pairs += int(count[0, rows_done // 128:(rows_done + chunk) // 128]
+                     .sum())
+        rows_done += chunk
+        if time.perf_counter() - t0 > seconds_hint:
+            break
+    elapsed = time.perf_counter() - t0
+    tflops = pairs * OPS_PER_PAIR / elapsed / 1e12
+    return {'value': tflops, 'unit': 'TFLOPS', 'cores': threads,
+            'kind': 'port', 'seconds': elapsed,
+            'sample': f'1 of 24 heads, {rows_done} of {SEQ} query rows: '
+                      'reference selection + fp32 masked attention '
+                      '(oracle numpy port of core/selection.py and '
+                      'core/reference.py), '
+                      f'{threads} host threads'}
+
+
+# ---------------------------------------------------------------- main
+
+def run_reference(args, rank: int):
+    if rank != 0:
+        return
+    samples = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_reference(seconds_hint=4.0)
+        if i >= args.warmup:
+            samples.append(r)
+    value = statistics.median(r['value'] for r in samples)
+    ms = statistics.median(r['seconds'] for r in samples) * 1e3
+    line = {'metric': METRIC, 'value': value, 'unit': 'TFLOPS',
+            'impl': 'reference', 'n_gpus': args.gpus, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms,
+            'higher_is_better': True, 'scaling': 'strong',
+            'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+            'config': {'workload': WORKLOAD, 'sample': samples[0]['sample']},
+            'cpu_baseline': {'value': value, 'unit': 'TFLOPS',
+                             'cores': samples[0]['cores'], 'kind': 'port',
+                             'sample': samples[0]['sample']},
+            'e2e': {'value': value, 'unit': 'TFLOPS',
+                    'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get('RANK', 0))
+    world = int(os.environ.get('WORLD_SIZE', 1))
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    if args.impl == 'reference':
+        run_reference(args, rank)
+        return
+    if args.warmup < 3:
+        raise SystemExit('--warmup must be at least 3')
+    device = torch.device('cuda', local)
+    torch.cuda.set_device(device)
+    group = None
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group(
+            'nccl', device_id=device, timeout=datetime.timedelta(seconds=120))
+        group = torch.distributed.group.WORLD
+    if HEADS % world:
+        raise SystemExit(f'{HEADS} heads do not split over {world} GPUs')
+    n_local = HEADS // world
+    heads = range(rank * n_local, (rank + 1) * n_local)
+
+    per_set = 3 * SEQ * n_local * DIM * 2
+    n_sets = max(2, math.ceil(3 * L2_BYTES / per_set) + 1)
+    sets = [make_set(i, heads, device) for i in range(n_sets)]
+    call = Call(n_local, device, group, world)
+
+    # exact algorithmic work: kept (query tile, key tile) pairs per set
+    pairs = []
+    for s in sets:
+        count = call(s)
+        pairs.append(int(count.sum().item()))
+    torch.cuda.synchronize()
+
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)]
+              for _ in range(args.steps)]
+    start, end = torch.cuda.Event(True), torch.cuda.Event(True)
+    with ClockSampler(local) as clocks:
+        # warm-up inside the sampler, so the clocks are sampled under load
+        for i in range(args.warmup):
+            call(sets[i % n_sets])
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(args.steps):
+            call(sets[i % n_sets], events[i])
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+    total_ms = start.elapsed_time(end)
+    phases = np.array([[e[j].elapsed_time(e[j + 1]) for j in range(4)]
+                       for e in events])             # steps x 4
+    work_pairs = sum(pairs[i % n_sets] for i in range(args.steps))
+
+    # ---- e2e: host buffers in, result out, inside the timed region
+    host = {k: sets[0][k].cpu().pin_memory() for k in ('q', 'k', 'v',
+                                                       'scores')}
+    dev = {k: torch.empty_like(sets[0][k]) for k in host}
+    out_host = torch.empty(SEQ, n_local, DIM, dtype=torch.bfloat16
+                           ).pin_memory()
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        for k in host:
+            dev[k].copy_(host[k], non_blocking=True)
+        call(dev)
+        out_host.copy_(call.out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    es, ee = torch.cuda.Event(True), torch.cuda.Event(True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    es.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    ee.record()
+    torch.cuda.synchronize()
+    e2e_ms = es.elapsed_time(ee) / e2e_steps
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    # ---- max over ranks
+    stats = torch.tensor([total_ms / args.steps, e2e_ms,
+                          *phases.mean(0).tolist()], dtype=torch.float64,
+                         device=device)
+    sums = torch.tensor([float(work_pairs), float(pairs[0]), float(h2d),
+                         float(d2h)], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(stats, torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(sums, torch.distributed.ReduceOp.SUM)
+    ms_step, e2e_ms = float(stats[0]), float(stats[1])
+    select_ms, quant_ms, attn_ms, gather_ms = (float(x) for x in stats[2:6])
+    total_pairs, e2e_pairs, h2d_all, d2h_all = (float(x) for x in sums)
+
+    if rank == 0:
+        peaks = measured_peaks()
+        int8_tops = measure_int8_peak(device)
+        bf16 = peaks['bf16_tflops']
+        mixed_peak = 2.0 / (1.0 / int8_tops + 1.0 / bf16)
+        ops_step = total_pairs / args.steps * OPS_PER_PAIR
+        value = ops_step / (ms_step * 1e-3) / 1e12
+        # the attention kernel on rank 0: its own pairs over its own time
+        attn_ops = work_pairs / args.steps * OPS_PER_PAIR
+        achieved = attn_ops / (attn_ms * 1e-3) / 1e12
+        traffic = profile_traffic()
+        line = {
+            'metric': METRIC, 'value': value, 'unit': 'TFLOPS',
+            'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': ms_step, 'higher_is_better': True,
+            'scaling': 'strong', 'vs_baseline': None, 'dtype': 'int8+bf16',
+            'data': 'synthetic',
+            'config': {'workload': WORKLOAD, 'heads': HEADS,
+                       'seq_len': SEQ, 'real_tokens': REAL,
+                       'kept_tiles_per_row': KEEP,
+                       'kept_pairs_per_call': total_pairs / args.steps,
+                       'parallelism': f'heads/{world}',
+                       'l2': f'{n_sets} rotating input sets of '
+                             f'{per_set / 2**20:.0f} MB per rank '
+                             f'(> L2 between reuses)'},
+            'breakdown_ms': {'select': select_ms, 'quant': quant_ms,
+                             'attention': attn_ms, 'all_gather': gather_ms},
+            'roofline': {
+                'bound': 'tensor', 'kernel': 'sparse_attention_kernel',
+                'achieved': achieved, 'peak': mixed_peak,
+                'unit': 'TFLOP/s', 'frac': achieved / mixed_peak,
+                'traffic': traffic,
+                'peak_note': (f'harmonic mix of measured INT8 '
+                              f'{int8_tops:.0f} TOPS (torch._int_mm 8192^3, '
+                              f'best of 10, this run) and bf16 {bf16} '
+                              f'TFLOPS ({peaks["source"]}): equal INT8 and '
+                              f'16-bit work per tile pair')},
+            'e2e': {'value': e2e_pairs * OPS_PER_PAIR / (e2e_ms * 1e-3) /
+                    1e12, 'unit': 'TFLOPS', 'ms_per_step': e2e_ms,
+                    'h2d_bytes_per_step': int(h2d_all),
+                    'd2h_bytes_per_step': int(d2h_all)},
+            'gpu_launches': 3 * args.steps,
+            'clocks': clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line['cpu_baseline'] = cpu_reference()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()
