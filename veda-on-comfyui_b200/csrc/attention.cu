@@ -198,6 +198,36 @@ __device__ void store_row(VT* dst, const float* v) {
   }
 }
 
+// Per-tile constants of the softmax: the two K-half scales folded with the
+// Q scale, the magic-number offsets that go with them, the valid rows.
+struct TileMeta {
+  float sc0, sc1;    // q_scale * k_scale of key rows 0-63 / 64-127
+  float off0, off1;  // 1.5 * 2^23 * sc0 / sc1
+  int valid;
+};
+
+// int32 S + 0x4B400000, read as fp32, is exactly 1.5 * 2^23 + S for
+// |S| < 2^22 (|S| <= 128 * 127 * 127 here), so S * sc - m comes out of one
+// fused multiply-add on the biased value: (1.5 * 2^23 + S) * sc - (off + m).
+// The only rounding beyond the reference's fp32 product is that of
+// off + m, at most 0.75 units of S, against the ~10^2 units of noise the
+// INT8 quantisation itself puts into S.
+constexpr uint32_t kMagicBits = 0x4B400000u;
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+
+__device__ __forceinline__ TileMeta load_meta(const float* ks_head,
+                                              const int32_t* valid, float qs,
+                                              int t) {
+  const float2 ks = __ldg(reinterpret_cast<const float2*>(ks_head + 2 * t));
+  TileMeta m;
+  m.sc0 = qs * ks.x;
+  m.sc1 = qs * ks.y;
+  m.off0 = kMagic * m.sc0;
+  m.off1 = kMagic * m.sc1;
+  m.valid = __ldg(valid + t);
+  return m;
+}
+
 template <typename VT>
 __device__ void softmax_rows(Barriers& b, uint32_t tmem, const int32_t* idx,
                              int count, int head, int qt, int warp, int lane,
@@ -213,13 +243,20 @@ __device__ void softmax_rows(Barriers& b, uint32_t tmem, const int32_t* idx,
             static_cast<int64_t>(qt * kTile + row) * p.out_sn +
             static_cast<int64_t>(head) * p.out_sh;
 
+  // Metadata runs ahead of the walk: tile ids two steps, scales one step,
+  // so no global load latency sits between two tiles.
+  TileMeta cur = load_meta(ks_head, p.valid, qs,
+                           clamp_tile(__ldg(idx), p.n_tiles));
+  int t_next = count > 1 ? clamp_tile(__ldg(idx + 1), p.n_tiles) : 0;
+
   float m = -1e30f, l = 0.0f;
   bool ok = true;
   for (int j = 0; j < count; ++j) {
-    const int t = clamp_tile(__ldg(idx + j), p.n_tiles);
-    const float sc0 = qs * __ldg(ks_head + 2 * t);
-    const float sc1 = qs * __ldg(ks_head + 2 * t + 1);
-    const int valid = __ldg(p.valid + t);
+    TileMeta next = cur;
+    int t_after = 0;
+    if (j + 1 < count) next = load_meta(ks_head, p.valid, qs, t_next);
+    if (j + 2 < count) t_after = clamp_tile(__ldg(idx + j + 2), p.n_tiles);
+
     ok = mbar_wait(&b.s_full, j & 1, abort, p.status, VEDA_STATUS_TIMEOUT);
     if (!__all_sync(0xffffffffu, ok)) {
       ok = false;
@@ -235,14 +272,24 @@ __device__ void softmax_rows(Barriers& b, uint32_t tmem, const int32_t* idx,
     reg_fence32(r + 32);
     reg_fence32(r + 64);
     reg_fence32(r + 96);
-    float x[128];
-    float mt = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < 128; ++c) {
-      x[c] = static_cast<float>(static_cast<int32_t>(r[c])) * (c < 64 ? sc0 : sc1);
-      if (valid < kTile && c >= valid) x[c] = -INFINITY;
-      mt = fmaxf(mt, x[c]);
+    for (int c = 0; c < 128; ++c) r[c] += kMagicBits;
+    if (cur.valid < kTile) {
+#pragma unroll
+      for (int c = 0; c < 128; ++c)
+        if (c >= cur.valid) r[c] = 0xFF800000u;  // -inf: never the max, p = 0
     }
+    // row max of each 64-column half on the biased values (monotone in S)
+    float ma0 = -INFINITY, mb0 = -INFINITY, ma1 = -INFINITY, mb1 = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 64; c += 4) {
+      ma0 = max3(ma0, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
+      mb0 = max3(mb0, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
+      ma1 = max3(ma1, __uint_as_float(r[c + 64]), __uint_as_float(r[c + 65]));
+      mb1 = max3(mb1, __uint_as_float(r[c + 66]), __uint_as_float(r[c + 67]));
+    }
+    const float mt = fmaxf(fmaf(fmaxf(ma0, mb0), cur.sc0, -cur.off0),
+                           fmaf(fmaxf(ma1, mb1), cur.sc1, -cur.off1));
     const bool need = mt > m + kRescaleThreshold;
     float alpha = 1.0f;
     if (need) {
@@ -250,35 +297,58 @@ __device__ void softmax_rows(Barriers& b, uint32_t tmem, const int32_t* idx,
       m = mt;
       l *= alpha;
     }
+    const uint64_t s0 = f2(cur.sc0, cur.sc0), s1 = f2(cur.sc1, cur.sc1);
+    const float c0 = -(cur.off0 + m), c1 = -(cur.off1 + m);
+    const uint64_t n0 = f2(c0, c0), n1 = f2(c1, c1);
+    uint64_t acc[4] = {0, 0, 0, 0};
+    uint32_t pk[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const uint64_t z =
+          fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+               i < 32 ? s0 : s1, i < 32 ? n0 : n1);
+      float z0, z1;
+      f2_split(z, z0, z1);
+      const float p0 = ex2_approx(z0), p1 = ex2_approx(z1);
+      acc[i & 3] = add2(acc[i & 3], f2(p0, p1));
+      pk[i] = Pack<VT>::two(p0, p1);
+    }
+    tmem_st32(lane_addr + kTmemS + 0, pk);
+    tmem_st32(lane_addr + kTmemS + 32, pk + 32);
+    {
+      float a0, a1, a2, a3, a4, a5, a6, a7;
+      f2_split(acc[0], a0, a1);
+      f2_split(acc[1], a2, a3);
+      f2_split(acc[2], a4, a5);
+      f2_split(acc[3], a6, a7);
+      l += ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
+    }
+    // O (from the previous tiles' P V, complete: the MMA warp waited for it
+    // before this tile's Q K^T) is rescaled when some row's max grew.
     if (j > 0 && __any_sync(0xffffffffu, need)) {
+      const uint64_t a2v = f2(alpha, alpha);
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         uint32_t o[32];
         tmem_ld32(lane_addr + kTmemO + 32 * cc, o);
         tmem_ld_wait(o);
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
-          o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+        for (int c = 0; c < 32; c += 2) {
+          float x0, x1;
+          f2_split(mul2(f2(__uint_as_float(o[c]), __uint_as_float(o[c + 1])),
+                        a2v), x0, x1);
+          o[c] = __float_as_uint(x0);
+          o[c + 1] = __float_as_uint(x1);
+        }
         tmem_st32(lane_addr + kTmemO + 32 * cc, o);
       }
-      tmem_st_wait();
     }
-    uint32_t pk[64];
-    float lsum = 0.0f;
-#pragma unroll
-    for (int c = 0; c < 64; ++c) {
-      const float p0 = ex2_approx(x[2 * c] - m);
-      const float p1 = ex2_approx(x[2 * c + 1] - m);
-      lsum += p0 + p1;
-      pk[c] = Pack<VT>::two(p0, p1);
-    }
-    l += lsum;
-    tmem_st32(lane_addr + kTmemS + 0, pk);
-    tmem_st32(lane_addr + kTmemS + 32, pk + 32);
     tmem_st_wait();
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&b.p_full);
+    cur = next;
+    t_next = t_after;
   }
   if (ok && count > 0)
     ok = mbar_wait(&b.o_full, (count - 1) & 1, abort, p.status,
