@@ -6,19 +6,30 @@
 // folded in, so these are base-2 logits); key columns at or past the tile's
 // valid count are masked; online softmax with exp2; O += P V; out = O / l.
 //
-// B200 mapping, one CTA per (query tile, head), two CTAs per SM:
-//   warp 0      TMA producer: the Q tile once, then K (int8, 16 KB) and V
-//               (16-bit, 32 KB) of each listed key tile into 2-stage rings,
-//               128-byte swizzled, fetched by tile id from the index list.
-//   warp 1      TMEM allocator and single-thread MMA issuer:
-//               S(TMEM, s32) = Q K^T as 4 x tcgen05.mma kind::i8 (K = 32);
-//               O(TMEM, f32) += P(TMEM) V(smem) as 8 x kind::f16 (K = 16).
-//   warps 2-5   softmax, one query row per thread (TMEM lane = row): load
-//               the S row, scale, mask, running max with lazy rescaling of
-//               O (only when the max grows by > 2^8), exp2, write P as
-//               packed 16-bit pairs over the first 64 columns of S.
-// TMEM: 256 columns per CTA, S in [0, 128), O in [128, 256), P aliases S.
-// Every wait is bounded (VEDA_STATUS_TIMEOUT) and ends the CTA cleanly.
+// B200 mapping: a persistent CTA per SM (384 threads, 208 KB of shared
+// memory, all 512 TMEM columns) walks pairs of query tiles of one head, the
+// two tiles ("slots" A and B) each with its own key-tile list:
+//   warp 0       TMA producer: per pair the two Q tiles (int8, double
+//                buffered across pairs), then K (int8, 16 KB) and V
+//                (16-bit, 32 KB) of each listed key tile, A and B
+//                interleaved, into a 3-stage ring, 128-byte swizzled.
+//   warp 1       TMEM allocator and the single MMA-issuing thread, in the
+//                fixed order P_A V -> Q_A K' -> P_B V -> Q_B K' ...:
+//                S(TMEM, s32) = Q K^T as 4 x tcgen05.mma kind::i8 (K = 32),
+//                O(TMEM, f32) += P(TMEM) V(smem) as 8 x kind::f16 (K = 16).
+//                While one slot's softmax runs, the tensor core serves the
+//                other slot, so exp and MMA overlap.
+//   warps 4-7    softmax of slot A, warps 8-11 of slot B: one query row per
+//                thread (TMEM lane = row); load the S row, scale, mask,
+//                running max with lazy rescaling of O (only when the max
+//                grows by > 2^8), exp2, write P as packed 16-bit pairs over
+//                the first 64 columns of S; at the end of a tile's walk,
+//                normalise O and store the rows.
+// TMEM: S_A [0, 128), S_B [128, 256), O_A [256, 384), O_B [384, 512); P
+// aliases S. One thread issues every MMA and the tensor pipe runs them in
+// order, so a Q K^T cannot overwrite P before the P V that reads it, and a
+// commit after a Q K^T also covers the P V before it (O is complete
+// whenever S is ready). Every wait is bounded (VEDA_STATUS_TIMEOUT).
 #include <atomic>
 
 #include "common.cuh"
@@ -26,31 +37,43 @@
 namespace veda {
 namespace {
 
-constexpr int kAttnThreads = 192;
+constexpr int kAttnThreads = 384;
+constexpr int kSlots = 2;
+constexpr int kStages = 3;
 constexpr uint32_t kQBytes = kTile * kDim;      // int8 Q tile
 constexpr uint32_t kKBytes = kTile * kDim;      // int8 K tile
 constexpr uint32_t kVBytes = kTile * kDim * 2;  // 16-bit V tile
-constexpr uint32_t kSmemQ = 0;
-constexpr uint32_t kSmemK = kSmemQ + kQBytes;
-constexpr uint32_t kSmemV = kSmemK + 2 * kKBytes;
-constexpr uint32_t kSmemBar = kSmemV + 2 * kVBytes;
-constexpr uint32_t kSmemBytes = kSmemBar + 256;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kTmemS = 0;
-constexpr uint32_t kTmemO = 128;
+constexpr uint32_t kSmemQ = 0;                  // [slot][buffer] Q tiles
+constexpr uint32_t kSmemK = kSmemQ + 4 * kQBytes;
+constexpr uint32_t kSmemV = kSmemK + kStages * kKBytes;
+constexpr uint32_t kSmemBar = kSmemV + kStages * kVBytes;
+constexpr uint32_t kSmemBytes = kSmemBar + 512;
+constexpr uint32_t kTmemCols = 512;
 // O is rescaled only when a row's max grows by more than this (log2 units),
 // so P stays below 2^8 and the final O / l is unchanged.
 constexpr float kRescaleThreshold = 8.0f;
+// Register split (setmaxnreg): the producer / MMA warpgroup gives up
+// registers to the two softmax warpgroups. 384 threads launch with 168
+// each (64512); 128 x 64 + 256 x 216 = 63488 stays within that.
+constexpr uint32_t kLowRegs = 64;
+constexpr uint32_t kHighRegs = 216;
+
+__host__ __device__ constexpr uint32_t tmem_s(int slot) { return 128u * slot; }
+__host__ __device__ constexpr uint32_t tmem_o(int slot) {
+  return 256u + 128u * slot;
+}
 
 struct Barriers {
-  uint64_t q_full;
-  uint64_t k_full[2], k_empty[2];
-  uint64_t v_full[2], v_empty[2];
-  uint64_t s_full, p_full, o_full, fin;
+  uint64_t q_full[kSlots][2], q_empty[kSlots][2];
+  uint64_t k_full[kStages], k_empty[kStages];
+  uint64_t v_full[kStages], v_empty[kStages];
+  uint64_t s_full[kSlots], p_full[kSlots];
+  uint64_t o_ready[kSlots], o_free[kSlots];
+  uint64_t fin;
   uint32_t tmem_base;
   int abort;
 };
-static_assert(sizeof(Barriers) <= 256, "barrier block too large");
+static_assert(sizeof(Barriers) <= 512, "barrier block too large");
 
 struct AttnParams {
   const float* q_scale;  // [H][n_tiles]
@@ -60,7 +83,8 @@ struct AttnParams {
   const int32_t* valid;  // [n_tiles]
   void* out;
   int64_t out_sn, out_sh;
-  int n_tiles, width;
+  int n_tiles, width, heads;
+  int n_pairs;           // heads * ceil(n_tiles / 2)
   int32_t* status;
 };
 
@@ -83,6 +107,40 @@ struct Pack<__half> {
   }
 };
 
+// A pair of query tiles of one head; slot B is absent (qt >= n_tiles) for
+// the last pair of a head with an odd tile count.
+struct Pair {
+  int head;
+  int qt[kSlots];
+  int count[kSlots];       // kept key tiles, 0 when the slot is absent
+  const int32_t* idx[kSlots];
+};
+
+__device__ __forceinline__ Pair decode_pair(int w, const AttnParams& p) {
+  const int per_head = (p.n_tiles + 1) >> 1;
+  Pair pr;
+  pr.head = w / per_head;
+  const int first = 2 * (w - pr.head * per_head);
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s) {
+    const int qt = first + s;
+    pr.qt[s] = qt;
+    pr.count[s] = 0;
+    pr.idx[s] = nullptr;
+    if (qt < p.n_tiles) {
+      const int64_t row = static_cast<int64_t>(pr.head) * p.n_tiles + qt;
+      int c = __ldg(p.count + row);
+      if (c < 0 || c > p.width) {
+        if (threadIdx.x == 0) report(p.status, VEDA_STATUS_BAD_COUNT);
+        c = c < 0 ? 0 : p.width;
+      }
+      pr.count[s] = c;
+      pr.idx[s] = p.index + row * p.width;
+    }
+  }
+  return pr;
+}
+
 // Bounded wait that ignores the abort flag: used to drain copies and MMAs
 // this CTA issued before it exits.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity,
@@ -101,84 +159,163 @@ __device__ __forceinline__ int clamp_tile(int t, int n_tiles) {
   return (t < 0 || t >= n_tiles) ? 0 : t;
 }
 
+__device__ __forceinline__ uint8_t* q_tile(uint8_t* smem, int slot, int buf) {
+  return smem + kSmemQ + (2 * slot + buf) * kQBytes;
+}
+
+// Warp 0, one thread: Q tiles per pair, then K / V tiles in the order the
+// MMA thread consumes them (A and B interleaved, tile by tile).
 __device__ void produce(const CUtensorMap* qm, const CUtensorMap* km,
                         const CUtensorMap* vm, uint8_t* smem, Barriers& b,
-                        const int32_t* idx, int count, int head, int qt,
                         const AttnParams& p) {
   volatile int* abort = &b.abort;
   tma_prefetch(qm);
   tma_prefetch(km);
   tma_prefetch(vm);
   const int n_slots = p.n_tiles * kTile;
-  mbar_expect_tx(&b.q_full, kQBytes);
-  tma_load_2d(qm, smem + kSmemQ, &b.q_full, 0, head * n_slots + qt * kTile);
-  int k_issued = 0, v_issued = 0;
-  for (int j = 0; j < count; ++j) {
-    int t = __ldg(idx + j);
-    if (t < 0 || t >= p.n_tiles) report(p.status, VEDA_STATUS_BAD_INDEX);
-    t = clamp_tile(t, p.n_tiles);
-    const int s = j & 1;
-    const uint32_t ph = (j >> 1) & 1;
-    if (!mbar_wait(&b.k_empty[s], ph ^ 1, abort, p.status, VEDA_STATUS_TIMEOUT))
-      break;
-    mbar_expect_tx(&b.k_full[s], kKBytes);
-    tma_load_2d(km, smem + kSmemK + s * kKBytes, &b.k_full[s], 0,
-                head * n_slots + t * kTile);
-    k_issued = j + 1;
-    if (!mbar_wait(&b.v_empty[s], ph ^ 1, abort, p.status, VEDA_STATUS_TIMEOUT))
-      break;
-    mbar_expect_tx(&b.v_full[s], kVBytes);
-    uint8_t* vdst = smem + kSmemV + s * kVBytes;
-    tma_load_3d(vm, vdst, &b.v_full[s], 0, head, t * kTile);
-    tma_load_3d(vm, vdst + kVBytes / 2, &b.v_full[s], 64, head, t * kTile);
-    v_issued = j + 1;
+  int q_uses[kSlots][2] = {{0, 0}, {0, 0}};
+  int gk = 0, gv = 0;  // K / V tiles issued (ring positions)
+  bool ok = true;
+  int it = 0;
+  for (int w = blockIdx.x; ok && w < p.n_pairs; w += gridDim.x, ++it) {
+    const Pair pr = decode_pair(w, p);
+    const int buf = it & 1;
+    for (int s = 0; s < kSlots && ok; ++s) {
+      if (pr.count[s] == 0) continue;
+      ok = mbar_wait(&b.q_empty[s][buf], (q_uses[s][buf] & 1) ^ 1, abort,
+                     p.status, VEDA_STATUS_TIMEOUT);
+      if (!ok) break;
+      mbar_expect_tx(&b.q_full[s][buf], kQBytes);
+      tma_load_2d(qm, q_tile(smem, s, buf), &b.q_full[s][buf], 0,
+                  pr.head * n_slots + pr.qt[s] * kTile);
+      ++q_uses[s][buf];
+    }
+    const int steps = max(pr.count[0], pr.count[1]);
+    for (int j = 0; j < steps && ok; ++j) {
+      for (int s = 0; s < kSlots && ok; ++s) {
+        if (j >= pr.count[s]) continue;
+        int t = __ldg(pr.idx[s] + j);
+        if (t < 0 || t >= p.n_tiles) report(p.status, VEDA_STATUS_BAD_INDEX);
+        t = clamp_tile(t, p.n_tiles);
+        const int stage = gk % kStages;
+        const uint32_t ph = (gk / kStages) & 1;
+        ok = mbar_wait(&b.k_empty[stage], ph ^ 1, abort, p.status,
+                       VEDA_STATUS_TIMEOUT);
+        if (!ok) break;
+        mbar_expect_tx(&b.k_full[stage], kKBytes);
+        tma_load_2d(km, smem + kSmemK + stage * kKBytes, &b.k_full[stage], 0,
+                    pr.head * n_slots + t * kTile);
+        ++gk;
+        ok = mbar_wait(&b.v_empty[stage], ph ^ 1, abort, p.status,
+                       VEDA_STATUS_TIMEOUT);
+        if (!ok) break;
+        mbar_expect_tx(&b.v_full[stage], kVBytes);
+        uint8_t* vdst = smem + kSmemV + stage * kVBytes;
+        tma_load_3d(vm, vdst, &b.v_full[stage], 0, pr.head, t * kTile);
+        tma_load_3d(vm, vdst + kVBytes / 2, &b.v_full[stage], 64, pr.head,
+                    t * kTile);
+        ++gv;
+      }
+    }
   }
   // Let every copy this CTA started land before it can exit.
-  drain_wait(&b.q_full, 0, p.status);
-  for (int j = k_issued - 2; j < k_issued; ++j)
-    if (j >= 0) drain_wait(&b.k_full[j & 1], (j >> 1) & 1, p.status);
-  for (int j = v_issued - 2; j < v_issued; ++j)
-    if (j >= 0) drain_wait(&b.v_full[j & 1], (j >> 1) & 1, p.status);
+  for (int s = 0; s < kSlots; ++s)
+    for (int buf = 0; buf < 2; ++buf)
+      if (q_uses[s][buf] > 0)
+        drain_wait(&b.q_full[s][buf], (q_uses[s][buf] - 1) & 1, p.status);
+  for (int g = gk - kStages; g < gk; ++g)
+    if (g >= 0) drain_wait(&b.k_full[g % kStages], (g / kStages) & 1, p.status);
+  for (int g = gv - kStages; g < gv; ++g)
+    if (g >= 0) drain_wait(&b.v_full[g % kStages], (g / kStages) & 1, p.status);
 }
 
-__device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem, int count,
-                          uint32_t idesc_pv, const AttnParams& p) {
+// Warp 1, one thread: every tcgen05.mma of the CTA, in a fixed interleave
+// of the two slots.
+template <typename VT>
+__device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
+                          const AttnParams& p) {
   volatile int* abort = &b.abort;
   constexpr uint32_t idesc_qk = idesc(2, 1, 0, 128, 128);
-  const uint64_t q_desc = smem_desc_sw128(smem_u32(smem + kSmemQ), 16, 1024);
-  bool ok = mbar_wait(&b.q_full, 0, abort, p.status, VEDA_STATUS_TIMEOUT);
-  for (int j = 0; ok && j < count; ++j) {
-    const int s = j & 1;
-    const uint32_t ph = (j >> 1) & 1;
-    if (!mbar_wait(&b.k_full[s], ph, abort, p.status, VEDA_STATUS_TIMEOUT))
-      break;
-    // S and P share TMEM: the previous P V must be done before S is rewritten.
-    if (j > 0 &&
-        !mbar_wait(&b.o_full, (j - 1) & 1, abort, p.status, VEDA_STATUS_TIMEOUT))
-      break;
+  constexpr uint32_t idesc_pv = idesc(1, Pack<VT>::kFormat, 1, 128, 128);
+  int q_uses[kSlots][2] = {{0, 0}, {0, 0}};
+  int tiles[kSlots] = {0, 0};  // P tiles taken per slot (p_full phases)
+  int items[kSlots] = {0, 0};  // walks finished per slot (o_free phases)
+  int gk = 0, gv = 0;          // K / V ring positions
+  bool ok = true;
+
+  // S[s] = Q[s] K^T of the next K in the ring; frees the K stage, signals S.
+  auto qk = [&](int s, int buf) {
+    const int stage = gk % kStages;
+    if (!mbar_wait(&b.k_full[stage], (gk / kStages) & 1, abort, p.status,
+                   VEDA_STATUS_TIMEOUT))
+      return false;
     tc_fence_after();
+    const uint64_t q_desc =
+        smem_desc_sw128(smem_u32(q_tile(smem, s, buf)), 16, 1024);
     const uint64_t k_desc =
-        smem_desc_sw128(smem_u32(smem + kSmemK + s * kKBytes), 16, 1024);
+        smem_desc_sw128(smem_u32(smem + kSmemK + stage * kKBytes), 16, 1024);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk)  // K = 32 bytes per instruction
-      mma_i8_ss(tmem + kTmemS, q_desc + 2 * kk, k_desc + 2 * kk, idesc_qk,
+      mma_i8_ss(tmem + tmem_s(s), q_desc + 2 * kk, k_desc + 2 * kk, idesc_qk,
                 kk > 0 ? 1u : 0u);
-    tc_commit(&b.k_empty[s]);
-    tc_commit(&b.s_full);
-    if (!mbar_wait(&b.p_full, j & 1, abort, p.status, VEDA_STATUS_TIMEOUT))
-      break;
-    if (!mbar_wait(&b.v_full[s], ph, abort, p.status, VEDA_STATUS_TIMEOUT))
-      break;
+    tc_commit(&b.k_empty[stage]);
+    tc_commit(&b.s_full[s]);
+    ++gk;
+    return true;
+  };
+  // O[s] (+)= P[s] V of the next V in the ring; frees the V stage.
+  auto pv = [&](int s, bool accumulate) {
+    const int stage = gv % kStages;
+    if (!mbar_wait(&b.v_full[stage], (gv / kStages) & 1, abort, p.status,
+                   VEDA_STATUS_TIMEOUT))
+      return false;
     tc_fence_after();
     const uint64_t v_desc = smem_desc_sw128(
-        smem_u32(smem + kSmemV + s * kVBytes), kVBytes / 2, 1024);
+        smem_u32(smem + kSmemV + stage * kVBytes), kVBytes / 2, 1024);
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)  // 16 keys (8 TMEM columns of P) each
-      mma_f16_ts(tmem + kTmemO, tmem + kTmemS + 8 * kk,
+      mma_f16_ts(tmem + tmem_o(s), tmem + tmem_s(s) + 8 * kk,
                  v_desc + static_cast<uint64_t>(kk * 128), idesc_pv,
-                 (j > 0 || kk > 0) ? 1u : 0u);
-    tc_commit(&b.v_empty[s]);
-    tc_commit(&b.o_full);
+                 (accumulate || kk > 0) ? 1u : 0u);
+    tc_commit(&b.v_empty[stage]);
+    ++gv;
+    return true;
+  };
+
+  int it = 0;
+  for (int w = blockIdx.x; ok && w < p.n_pairs; w += gridDim.x, ++it) {
+    const Pair pr = decode_pair(w, p);
+    const int buf = it & 1;
+    for (int s = 0; s < kSlots && ok; ++s) {
+      if (pr.count[s] == 0) continue;
+      ok = mbar_wait(&b.q_full[s][buf], q_uses[s][buf] & 1, abort, p.status,
+                     VEDA_STATUS_TIMEOUT);
+      ++q_uses[s][buf];
+      if (ok) ok = qk(s, buf);
+    }
+    const int steps = max(pr.count[0], pr.count[1]);
+    for (int j = 0; j < steps && ok; ++j) {
+      for (int s = 0; s < kSlots && ok; ++s) {
+        if (j >= pr.count[s]) continue;
+        ok = mbar_wait(&b.p_full[s], tiles[s] & 1, abort, p.status,
+                       VEDA_STATUS_TIMEOUT);
+        ++tiles[s];
+        // the first P V of a walk overwrites O: the last walk's rows must
+        // have been read out of it
+        if (ok && j == 0 && items[s] > 0)
+          ok = mbar_wait(&b.o_free[s], (items[s] - 1) & 1, abort, p.status,
+                         VEDA_STATUS_TIMEOUT);
+        if (ok) ok = pv(s, j > 0);
+        if (!ok) break;
+        if (j + 1 < pr.count[s]) {
+          ok = qk(s, buf);
+        } else {
+          tc_commit(&b.o_ready[s]);
+          tc_commit(&b.q_empty[s][buf]);
+          ++items[s];
+        }
+      }
+    }
   }
   // Every MMA this CTA issued completes before TMEM is released.
   tc_commit(&b.fin);
@@ -229,147 +366,182 @@ __device__ __forceinline__ TileMeta load_meta(const float* ks_head,
 }
 
 template <typename VT>
-__device__ void softmax_rows(Barriers& b, uint32_t tmem, const int32_t* idx,
-                             int count, int head, int qt, int warp, int lane,
-                             const AttnParams& p) {
+__device__ void softmax_loop(int slot, Barriers& b, uint32_t tmem,
+                             const AttnParams& p, int warp, int lane) {
   volatile int* abort = &b.abort;
   const int quarter = warp & 3;  // TMEM lanes this warp may access
   const int row = quarter * 32 + lane;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-  const int64_t row_base = static_cast<int64_t>(head) * p.n_tiles + qt;
-  const float qs = __ldg(p.q_scale + row_base);
-  const float* ks_head = p.k_scale + static_cast<int64_t>(head) * 2 * p.n_tiles;
-  VT* out = static_cast<VT*>(p.out) +
-            static_cast<int64_t>(qt * kTile + row) * p.out_sn +
-            static_cast<int64_t>(head) * p.out_sh;
+  const uint32_t s_addr = lane_addr + tmem_s(slot);
+  const uint32_t o_addr = lane_addr + tmem_o(slot);
+  int tiles = 0, items = 0;  // phases of s_full / o_ready of this slot
+  bool good = true;
+  for (int w = blockIdx.x; good && w < p.n_pairs; w += gridDim.x) {
+    const Pair pr = decode_pair(w, p);
+    const int qt = pr.qt[slot];
+    if (qt >= p.n_tiles) continue;
+    const int count = pr.count[slot];
+    const int head = pr.head;
+    VT* out = static_cast<VT*>(p.out) +
+              static_cast<int64_t>(qt * kTile + row) * p.out_sn +
+              static_cast<int64_t>(head) * p.out_sh;
+    if (count == 0) {  // nothing kept: the reference's acc / 1 = 0
+#pragma unroll
+      for (int c = 0; c < kDim; c += 8)
+        *reinterpret_cast<uint4*>(out + c) = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const int32_t* idx = pr.idx[slot];
+    const float qs = __ldg(p.q_scale + static_cast<int64_t>(head) * p.n_tiles + qt);
+    const float* ks_head = p.k_scale + static_cast<int64_t>(head) * 2 * p.n_tiles;
+    // Metadata runs ahead of the walk: tile ids two steps, scales one
+    // step, so no global load latency sits between two tiles.
+    TileMeta cur = load_meta(ks_head, p.valid, qs,
+                             clamp_tile(__ldg(idx), p.n_tiles));
+    int t_next = count > 1 ? clamp_tile(__ldg(idx + 1), p.n_tiles) : 0;
 
-  // Metadata runs ahead of the walk: tile ids two steps, scales one step,
-  // so no global load latency sits between two tiles.
-  TileMeta cur = load_meta(ks_head, p.valid, qs,
-                           clamp_tile(__ldg(idx), p.n_tiles));
-  int t_next = count > 1 ? clamp_tile(__ldg(idx + 1), p.n_tiles) : 0;
+    float m = -1e30f, l = 0.0f;
+    for (int j = 0; j < count; ++j) {
+      TileMeta next = cur;
+      int t_after = 0;
+      if (j + 1 < count) next = load_meta(ks_head, p.valid, qs, t_next);
+      if (j + 2 < count) t_after = clamp_tile(__ldg(idx + j + 2), p.n_tiles);
 
-  float m = -1e30f, l = 0.0f;
-  bool ok = true;
-  for (int j = 0; j < count; ++j) {
-    TileMeta next = cur;
-    int t_after = 0;
-    if (j + 1 < count) next = load_meta(ks_head, p.valid, qs, t_next);
-    if (j + 2 < count) t_after = clamp_tile(__ldg(idx + j + 2), p.n_tiles);
-
-    ok = mbar_wait(&b.s_full, j & 1, abort, p.status, VEDA_STATUS_TIMEOUT);
-    if (!__all_sync(0xffffffffu, ok)) {
-      ok = false;
+      good = mbar_wait(&b.s_full[slot], tiles & 1, abort, p.status,
+                       VEDA_STATUS_TIMEOUT);
+      ++tiles;
+      if (!__all_sync(0xffffffffu, good)) {
+        good = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[128];
+      tmem_ld32(s_addr + 0, r);
+      tmem_ld32(s_addr + 32, r + 32);
+      tmem_ld32(s_addr + 64, r + 64);
+      tmem_ld32(s_addr + 96, r + 96);
+      tmem_ld_wait(r);
+      reg_fence32(r + 32);
+      reg_fence32(r + 64);
+      reg_fence32(r + 96);
+#pragma unroll
+      for (int c = 0; c < 128; ++c) r[c] += kMagicBits;
+      if (cur.valid < kTile) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c >= cur.valid) r[c] = 0xFF800000u;  // -inf: never the max, p = 0
+      }
+      // row max of each 64-column half on the biased values (monotone in S)
+      float ma0 = -INFINITY, mb0 = -INFINITY, ma1 = -INFINITY,
+            mb1 = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; c += 4) {
+        ma0 = max3(ma0, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
+        mb0 = max3(mb0, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
+        ma1 = max3(ma1, __uint_as_float(r[c + 64]), __uint_as_float(r[c + 65]));
+        mb1 = max3(mb1, __uint_as_float(r[c + 66]), __uint_as_float(r[c + 67]));
+      }
+      const float mt = fmaxf(fmaf(fmaxf(ma0, mb0), cur.sc0, -cur.off0),
+                             fmaf(fmaxf(ma1, mb1), cur.sc1, -cur.off1));
+      const bool need = mt > m + kRescaleThreshold;
+      float alpha = 1.0f;
+      if (need) {
+        alpha = ex2_approx(m - mt);
+        m = mt;
+        l *= alpha;
+      }
+      const uint64_t s0 = f2(cur.sc0, cur.sc0), s1 = f2(cur.sc1, cur.sc1);
+      const float c0 = -(cur.off0 + m), c1 = -(cur.off1 + m);
+      const uint64_t n0 = f2(c0, c0), n1 = f2(c1, c1);
+      uint64_t acc[4] = {0, 0, 0, 0};
+      uint32_t pk[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const uint64_t z =
+            fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+                 i < 32 ? s0 : s1, i < 32 ? n0 : n1);
+        float z0, z1;
+        f2_split(z, z0, z1);
+        const float p0 = ex2_approx(z0), p1 = ex2_approx(z1);
+        acc[i & 3] = add2(acc[i & 3], f2(p0, p1));
+        pk[i] = Pack<VT>::two(p0, p1);
+      }
+      tmem_st32(s_addr + 0, pk);
+      tmem_st32(s_addr + 32, pk + 32);
+      {
+        float a0, a1, a2, a3, a4, a5, a6, a7;
+        f2_split(acc[0], a0, a1);
+        f2_split(acc[1], a2, a3);
+        f2_split(acc[2], a4, a5);
+        f2_split(acc[3], a6, a7);
+        l += ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
+      }
+      // O holds the P V of every earlier tile of this walk (the commit
+      // that signalled S covered them) and is rescaled when a row's max
+      // grew.
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        const uint64_t a2v = f2(alpha, alpha);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + 32 * cc, o);
+          tmem_ld_wait(o);
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float x0, x1;
+            f2_split(mul2(f2(__uint_as_float(o[c]), __uint_as_float(o[c + 1])),
+                          a2v), x0, x1);
+            o[c] = __float_as_uint(x0);
+            o[c + 1] = __float_as_uint(x1);
+          }
+          tmem_st32(o_addr + 32 * cc, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b.p_full[slot]);
+      cur = next;
+      t_next = t_after;
+    }
+    if (!good) break;
+    good = mbar_wait(&b.o_ready[slot], items & 1, abort, p.status,
+                     VEDA_STATUS_TIMEOUT);
+    ++items;
+    if (!__all_sync(0xffffffffu, good)) {
+      good = false;
       break;
     }
     tc_fence_after();
-    uint32_t r[128];
-    tmem_ld32(lane_addr + kTmemS + 0, r);
-    tmem_ld32(lane_addr + kTmemS + 32, r + 32);
-    tmem_ld32(lane_addr + kTmemS + 64, r + 64);
-    tmem_ld32(lane_addr + kTmemS + 96, r + 96);
-    tmem_ld_wait(r);
-    reg_fence32(r + 32);
-    reg_fence32(r + 64);
-    reg_fence32(r + 96);
+    const float inv = l > 0.0f ? 1.0f / l : 1.0f;
 #pragma unroll
-    for (int c = 0; c < 128; ++c) r[c] += kMagicBits;
-    if (cur.valid < kTile) {
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t o[32];
+      tmem_ld32(o_addr + 32 * cc, o);
+      tmem_ld_wait(o);
+      float v[32];
 #pragma unroll
-      for (int c = 0; c < 128; ++c)
-        if (c >= cur.valid) r[c] = 0xFF800000u;  // -inf: never the max, p = 0
+      for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(o[c]) * inv;
+      store_row<VT>(out + 32 * cc, v);
     }
-    // row max of each 64-column half on the biased values (monotone in S)
-    float ma0 = -INFINITY, mb0 = -INFINITY, ma1 = -INFINITY, mb1 = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < 64; c += 4) {
-      ma0 = max3(ma0, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
-      mb0 = max3(mb0, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
-      ma1 = max3(ma1, __uint_as_float(r[c + 64]), __uint_as_float(r[c + 65]));
-      mb1 = max3(mb1, __uint_as_float(r[c + 66]), __uint_as_float(r[c + 67]));
-    }
-    const float mt = fmaxf(fmaf(fmaxf(ma0, mb0), cur.sc0, -cur.off0),
-                           fmaf(fmaxf(ma1, mb1), cur.sc1, -cur.off1));
-    const bool need = mt > m + kRescaleThreshold;
-    float alpha = 1.0f;
-    if (need) {
-      alpha = ex2_approx(m - mt);
-      m = mt;
-      l *= alpha;
-    }
-    const uint64_t s0 = f2(cur.sc0, cur.sc0), s1 = f2(cur.sc1, cur.sc1);
-    const float c0 = -(cur.off0 + m), c1 = -(cur.off1 + m);
-    const uint64_t n0 = f2(c0, c0), n1 = f2(c1, c1);
-    uint64_t acc[4] = {0, 0, 0, 0};
-    uint32_t pk[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const uint64_t z =
-          fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
-               i < 32 ? s0 : s1, i < 32 ? n0 : n1);
-      float z0, z1;
-      f2_split(z, z0, z1);
-      const float p0 = ex2_approx(z0), p1 = ex2_approx(z1);
-      acc[i & 3] = add2(acc[i & 3], f2(p0, p1));
-      pk[i] = Pack<VT>::two(p0, p1);
-    }
-    tmem_st32(lane_addr + kTmemS + 0, pk);
-    tmem_st32(lane_addr + kTmemS + 32, pk + 32);
-    {
-      float a0, a1, a2, a3, a4, a5, a6, a7;
-      f2_split(acc[0], a0, a1);
-      f2_split(acc[1], a2, a3);
-      f2_split(acc[2], a4, a5);
-      f2_split(acc[3], a6, a7);
-      l += ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
-    }
-    // O (from the previous tiles' P V, complete: the MMA warp waited for it
-    // before this tile's Q K^T) is rescaled when some row's max grew.
-    if (j > 0 && __any_sync(0xffffffffu, need)) {
-      const uint64_t a2v = f2(alpha, alpha);
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t o[32];
-        tmem_ld32(lane_addr + kTmemO + 32 * cc, o);
-        tmem_ld_wait(o);
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float x0, x1;
-          f2_split(mul2(f2(__uint_as_float(o[c]), __uint_as_float(o[c + 1])),
-                        a2v), x0, x1);
-          o[c] = __float_as_uint(x0);
-          o[c + 1] = __float_as_uint(x1);
-        }
-        tmem_st32(lane_addr + kTmemO + 32 * cc, o);
-      }
-    }
-    tmem_st_wait();
+    // O of this slot may now be overwritten by the next walk's first P V.
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&b.p_full);
-    cur = next;
-    t_next = t_after;
-  }
-  if (ok && count > 0)
-    ok = mbar_wait(&b.o_full, (count - 1) & 1, abort, p.status,
-                   VEDA_STATUS_TIMEOUT);
-  if (!__all_sync(0xffffffffu, ok)) return;
-  tc_fence_after();
-  const float inv = l > 0.0f ? 1.0f / l : 1.0f;
-#pragma unroll
-  for (int cc = 0; cc < 4; ++cc) {
-    uint32_t o[32];
-    tmem_ld32(lane_addr + kTmemO + 32 * cc, o);
-    tmem_ld_wait(o);
-    float v[32];
-#pragma unroll
-    for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(o[c]) * inv;
-    store_row<VT>(out + 32 * cc, v);
+    if (lane == 0) mbar_arrive(&b.o_free[slot]);
   }
 }
 
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 template <typename VT>
-__global__ void __launch_bounds__(kAttnThreads, 2)
+__global__ void __launch_bounds__(kAttnThreads, 1)
     sparse_attention_kernel(const __grid_constant__ CUtensorMap q_map,
                             const __grid_constant__ CUtensorMap k_map,
                             const __grid_constant__ CUtensorMap v_map,
@@ -377,29 +549,27 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   extern __shared__ __align__(1024) uint8_t smem[];
   Barriers& b = *reinterpret_cast<Barriers*>(smem + kSmemBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, head = blockIdx.y;
-  const int64_t row_base = static_cast<int64_t>(head) * p.n_tiles + qt;
-  int count = __ldg(p.count + row_base);
-  if (count < 0 || count > p.width) {
-    if (threadIdx.x == 0) report(p.status, VEDA_STATUS_BAD_COUNT);
-    count = count < 0 ? 0 : p.width;
-  }
-  const int32_t* idx = p.index + row_base * p.width;
 
   if (threadIdx.x == 0) {
     // The 128-byte swizzle pattern assumes 1024-byte aligned tiles.
     b.abort = (smem_u32(smem) & 1023u) != 0 ? 1 : 0;
     if (b.abort) report(p.status, VEDA_STATUS_MISALIGNED);
-    mbar_init(&b.q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&b.k_full[s], 1);
-      mbar_init(&b.k_empty[s], 1);
-      mbar_init(&b.v_full[s], 1);
-      mbar_init(&b.v_empty[s], 1);
+    for (int s = 0; s < kSlots; ++s) {
+      for (int buf = 0; buf < 2; ++buf) {
+        mbar_init(&b.q_full[s][buf], 1);
+        mbar_init(&b.q_empty[s][buf], 1);
+      }
+      mbar_init(&b.s_full[s], 1);
+      mbar_init(&b.p_full[s], 4);
+      mbar_init(&b.o_ready[s], 1);
+      mbar_init(&b.o_free[s], 4);
     }
-    mbar_init(&b.s_full, 1);
-    mbar_init(&b.p_full, 4);
-    mbar_init(&b.o_full, 1);
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(&b.k_full[st], 1);
+      mbar_init(&b.k_empty[st], 1);
+      mbar_init(&b.v_full[st], 1);
+      mbar_init(&b.v_empty[st], 1);
+    }
     mbar_init(&b.fin, 1);
     fence_mbar_init();
   }
@@ -408,29 +578,20 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = b.tmem_base;
-  const bool run = count > 0 && b.abort == 0;
+  const bool run = b.abort == 0;
 
-  if (run) {
-    if (warp == 0) {
-      if (lane == 0)
-        produce(&q_map, &k_map, &v_map, smem, b, idx, count, head, qt, p);
+  if (warp < 4) {
+    regs_dec<kLowRegs>();
+    if (run && warp == 0) {
+      if (lane == 0) produce(&q_map, &k_map, &v_map, smem, b, p);
       __syncwarp();
-    } else if (warp == 1) {
-      if (lane == 0)
-        issue_mma(smem, b, tmem, count,
-                  idesc(1, Pack<VT>::kFormat, 1, 128, 128), p);
+    } else if (run && warp == 1) {
+      if (lane == 0) issue_mma<VT>(smem, b, tmem, p);
       __syncwarp();
-    } else {
-      softmax_rows<VT>(b, tmem, idx, count, head, qt, warp, lane, p);
     }
-  } else if (warp >= 2 && count == 0) {
-    const int row = (warp & 3) * 32 + lane;
-    VT* out = static_cast<VT*>(p.out) +
-              static_cast<int64_t>(qt * kTile + row) * p.out_sn +
-              static_cast<int64_t>(head) * p.out_sh;
-#pragma unroll
-    for (int c = 0; c < kDim; c += 8)
-      *reinterpret_cast<uint4*>(out + c) = make_uint4(0, 0, 0, 0);
+  } else {
+    regs_inc<kHighRegs>();
+    if (run) softmax_loop<VT>((warp - 4) >> 2, b, tmem, p, warp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -441,22 +602,27 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 }
 
 std::atomic<uint32_t> g_smem_set[2][64];
+std::atomic<int> g_sm_count[64];
 
 template <typename VT>
 int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
-           const AttnParams& p, int heads, cudaStream_t stream, int dt) {
+           const AttnParams& p, cudaStream_t stream, int dt) {
   const int device = current_device();
-  if (device >= 0 && device < 64 && !g_smem_set[dt][device].load()) {
-    VEDA_CHECK_CUDA(cudaFuncSetAttribute(
-        sparse_attention_kernel<VT>,
-        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    g_smem_set[dt][device].store(1);
-  } else if (device >= 64) {
-    VEDA_CHECK_CUDA(cudaFuncSetAttribute(
-        sparse_attention_kernel<VT>,
-        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  int sms = 148;
+  if (device >= 0 && device < 64 && g_sm_count[device].load() > 0) {
+    sms = g_sm_count[device].load();
+  } else {
+    VEDA_CHECK_CUDA(cudaDeviceGetAttribute(
+        &sms, cudaDevAttrMultiProcessorCount, device));
+    if (device >= 0 && device < 64) g_sm_count[device].store(sms);
   }
-  dim3 grid(p.n_tiles, heads);
+  if (device < 0 || device >= 64 || !g_smem_set[dt][device].load()) {
+    VEDA_CHECK_CUDA(cudaFuncSetAttribute(
+        sparse_attention_kernel<VT>,
+        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    if (device >= 0 && device < 64) g_smem_set[dt][device].store(1);
+  }
+  const int grid = p.n_pairs < sms ? p.n_pairs : sms;
   sparse_attention_kernel<VT><<<grid, kAttnThreads, kSmemBytes, stream>>>(
       qm, km, vm, p);
   VEDA_CHECK_CUDA(cudaGetLastError());
@@ -531,9 +697,10 @@ extern "C" int veda_sparse_attention(
   p.out_sh = out_stride_h;
   p.n_tiles = n_tiles;
   p.width = width;
+  p.heads = heads;
+  p.n_pairs = heads * ((n_tiles + 1) / 2);
   p.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (v_dtype == VEDA_BF16)
-    return launch<__nv_bfloat16>(qm, km, vm, p, heads, s, 0);
-  return launch<__half>(qm, km, vm, p, heads, s, 1);
+  if (v_dtype == VEDA_BF16) return launch<__nv_bfloat16>(qm, km, vm, p, s, 0);
+  return launch<__half>(qm, km, vm, p, s, 1);
 }
