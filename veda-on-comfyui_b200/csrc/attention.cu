@@ -153,7 +153,7 @@ __device__ __forceinline__ Item decode_item(int w, const AttnParams& p) {
 // stage g % 3.
 
 // Warp 0, one thread: the Q tile of each item, then its K / V tiles.
-__device__ void produce(const CUtensorMap* qm, const CUtensorMap* km,
+__device__ __forceinline__ void produce(const CUtensorMap* qm, const CUtensorMap* km,
                         const CUtensorMap* vm, uint8_t* smem, Barriers& b,
                         const AttnParams& p) {
   volatile int* abort = &b.abort;
@@ -173,8 +173,10 @@ __device__ void produce(const CUtensorMap* qm, const CUtensorMap* km,
     tma_load_2d(qm, smem + kSmemQ + (n & 1) * kQBytes, &b.q_full[n & 1], 0,
                 it.head * n_slots + it.qt * kTile);
     ++n;
+    int t_raw = __ldg(it.idx);
     for (int j = 0; j < it.count && ok; ++j) {
-      int t = __ldg(it.idx + j);
+      int t = t_raw;
+      if (j + 1 < it.count) t_raw = __ldg(it.idx + j + 1);  // used next step
       if (t < 0 || t >= p.n_tiles) report(p.status, VEDA_STATUS_BAD_INDEX);
       t = clamp_tile(t, p.n_tiles);
       const int stage = gk % kStages;
@@ -208,7 +210,7 @@ __device__ void produce(const CUtensorMap* qm, const CUtensorMap* km,
 
 // Warp 2, one thread: S[g % 2] = Q K^T for every tile g, as soon as its K
 // is in and both halves' P V that last read S[g % 2] (tile g - 2) are done.
-__device__ void issue_qk(uint8_t* smem, Barriers& b, uint32_t tmem,
+__device__ __forceinline__ void issue_qk(uint8_t* smem, Barriers& b, uint32_t tmem,
                          const AttnParams& p) {
   volatile int* abort = &b.abort;
   constexpr uint32_t idesc_qk = idesc(2, 1, 0, 128, 128);
@@ -252,7 +254,7 @@ __device__ void issue_qk(uint8_t* smem, Barriers& b, uint32_t tmem,
 // g once that half's P is written; the first P V of an item waits until
 // the previous item's rows have been read out of O_0 and O_1.
 template <typename VT>
-__device__ void issue_pv(uint8_t* smem, Barriers& b, uint32_t tmem,
+__device__ __forceinline__ void issue_pv(uint8_t* smem, Barriers& b, uint32_t tmem,
                          const AttnParams& p) {
   volatile int* abort = &b.abort;
   constexpr uint32_t idesc_pv = idesc(1, Pack<VT>::kFormat, 1, 128, 128);
@@ -342,15 +344,146 @@ __device__ __forceinline__ TileMeta load_meta(const float* ks_head,
 // Warps 4-7 (key half 0) and 8-11 (key half 1): the softmax of one half of
 // every tile of every item, one row per thread; at the end of each walk the
 // two halves are merged and each warpgroup stores its 64 output columns.
+//
+// The global loads that feed a tile (its K scales and valid count, and the
+// id of the tile after it) are issued a step ahead and consumed a step
+// later, so their latency never sits between two tiles.
 template <typename VT>
-__device__ void softmax_loop(int h, uint8_t* smem, Barriers& b, uint32_t tmem,
+struct HalfSoftmax {
+  Barriers& b;
+  const AttnParams& p;
+  uint32_t lane_addr, o_self;
+  int h, lane;
+  // per walk
+  const int32_t* idx;
+  const float* ks_head;
+  float qs;
+  int count;
+  float m, l;
+  // metadata pipeline (raw values, used one step after their load)
+  float2 ks_cur, ks_next;
+  int valid_cur, valid_next, raw_t1, raw_t2;
+
+  __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) {
+    bool ok = mbar_wait(bar, parity, &b.abort, p.status, VEDA_STATUS_TIMEOUT);
+    return __all_sync(0xffffffffu, ok);
+  }
+
+  __device__ __forceinline__ void load_s(int g, uint32_t* r) {
+    const uint32_t a = lane_addr + tmem_s(g & 1) + 64 * h;
+    tmem_ld32(a, r);
+    tmem_ld32(a + 32, r + 32);
+  }
+
+  // One tile: r holds its S (loaded), rn receives the next tile's S.
+  __device__ __forceinline__ bool step(int j, int g, uint32_t* r,
+                                       uint32_t* rn) {
+    const int t1 = clamp_tile(raw_t1, p.n_tiles);
+    if (j + 1 < count) {
+      ks_next = __ldg(reinterpret_cast<const float2*>(ks_head + 2 * t1));
+      valid_next = __ldg(p.valid + t1);
+    }
+    if (j + 2 < count) raw_t2 = __ldg(idx + j + 2);
+    const float sc = qs * (h ? ks_cur.y : ks_cur.x);
+    const float off = kMagic * sc;
+
+#pragma unroll
+    for (int c = 0; c < 64; ++c) r[c] += kMagicBits;
+    if (valid_cur < 64 * h + 64) {
+#pragma unroll
+      for (int c = 0; c < 64; ++c)
+        if (64 * h + c >= valid_cur) r[c] = 0xFF800000u;  // -inf, p = 0
+    }
+    float ma = -INFINITY, mb = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 64; c += 4) {
+      ma = max3(ma, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
+      mb = max3(mb, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
+    }
+    const float mt = fmaf(fmaxf(ma, mb), sc, -off);  // this half's max logit
+    const bool need = mt > m + kRescaleThreshold;
+    float alpha = 1.0f;
+    if (need) {
+      alpha = ex2_approx(m - mt);
+      m = mt;
+      l *= alpha;
+    }
+    const uint64_t s2 = f2(sc, sc);
+    const float cn = -(off + m);
+    const uint64_t n2 = f2(cn, cn);
+    uint64_t acc[4] = {0, 0, 0, 0};
+    uint32_t pk[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const uint64_t z =
+          fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+               s2, n2);
+      float z0, z1;
+      f2_split(z, z0, z1);
+      const float p0 = ex2_approx(z0), p1 = ex2_approx(z1);
+      acc[i & 3] = add2(acc[i & 3], f2(p0, p1));
+      pk[i] = Pack<VT>::two(p0, p1);
+    }
+    tmem_st32(lane_addr + tmem_s(g & 1) + 64 * h, pk);
+    {
+      float a0, a1, a2, a3, a4, a5, a6, a7;
+      f2_split(acc[0], a0, a1);
+      f2_split(acc[1], a2, a3);
+      f2_split(acc[2], a4, a5);
+      f2_split(acc[3], a6, a7);
+      l += ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
+    }
+    // A grown max rescales O_h, which must first hold this half's P V of
+    // the previous tile (rare after the first tiles of a walk).
+    if (j > 0 && __any_sync(0xffffffffu, need)) {
+      if (!wait(&b.pv_done[h][(g - 1) & 1], ((g - 1) >> 1) & 1)) return false;
+      tc_fence_after();
+      const uint64_t a2v = f2(alpha, alpha);
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t o[32];
+        tmem_ld32(o_self + 32 * cc, o);
+        tmem_ld_wait(o);
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float x0, x1;
+          f2_split(mul2(f2(__uint_as_float(o[c]), __uint_as_float(o[c + 1])),
+                        a2v), x0, x1);
+          o[c] = __float_as_uint(x0);
+          o[c + 1] = __float_as_uint(x1);
+        }
+        tmem_st32(o_self + 32 * cc, o);
+      }
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&b.p_full[h][g & 1]);
+    if (j + 1 < count) {
+      if (!wait(&b.s_full[(g + 1) & 1], ((g + 1) >> 1) & 1)) return false;
+      tc_fence_after();
+      load_s(g + 1, rn);
+      tmem_ld_wait(rn);
+      reg_fence32(rn + 32);
+    }
+    ks_cur = ks_next;
+    valid_cur = valid_next;
+    raw_t1 = raw_t2;
+    return true;
+  }
+};
+
+template <typename VT>
+__device__ __forceinline__ void softmax_loop(int h, uint8_t* smem, Barriers& b, uint32_t tmem,
                              const AttnParams& p, int warp, int lane) {
-  volatile int* abort = &b.abort;
   const int quarter = warp & 3;  // TMEM lanes this warp may access
   const int row = quarter * 32 + lane;
-  const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-  const uint32_t o_self = lane_addr + tmem_o(h);
-  const uint32_t o_other = lane_addr + tmem_o(h ^ 1);
+  HalfSoftmax<VT> sm{b, p};
+  sm.lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+  sm.o_self = sm.lane_addr + tmem_o(h);
+  sm.h = h;
+  sm.lane = lane;
+  const uint32_t o_other = sm.lane_addr + tmem_o(h ^ 1);
   float2* xch = reinterpret_cast<float2*>(smem + kSmemXch);
   int n = 0, g = 0;
   bool good = true;
@@ -365,142 +498,49 @@ __device__ void softmax_loop(int h, uint8_t* smem, Barriers& b, uint32_t tmem,
         *reinterpret_cast<uint4*>(out + c) = make_uint4(0, 0, 0, 0);
       continue;
     }
-    const float qs = __ldg(p.q_scale + static_cast<int64_t>(it.head) * p.n_tiles + it.qt);
-    const float* ks_head = p.k_scale + static_cast<int64_t>(it.head) * 2 * p.n_tiles;
-    // Metadata runs ahead of the walk: tile ids two steps, scales one
-    // step, so no global load latency sits between two tiles.
-    TileMeta cur = load_meta(ks_head, p.valid, qs,
-                             clamp_tile(__ldg(it.idx), p.n_tiles));
-    int t_next = it.count > 1 ? clamp_tile(__ldg(it.idx + 1), p.n_tiles) : 0;
+    sm.idx = it.idx;
+    sm.count = it.count;
+    sm.qs = __ldg(p.q_scale + static_cast<int64_t>(it.head) * p.n_tiles + it.qt);
+    sm.ks_head = p.k_scale + static_cast<int64_t>(it.head) * 2 * p.n_tiles;
+    const int t0 = clamp_tile(__ldg(it.idx), p.n_tiles);
+    sm.ks_cur = __ldg(reinterpret_cast<const float2*>(sm.ks_head + 2 * t0));
+    sm.valid_cur = __ldg(p.valid + t0);
+    sm.raw_t1 = it.count > 1 ? __ldg(it.idx + 1) : 0;
+    sm.ks_next = sm.ks_cur;
+    sm.valid_next = sm.valid_cur;
+    sm.raw_t2 = 0;
+    sm.m = -1e30f;
+    sm.l = 0.0f;
 
-    float m = -1e30f, l = 0.0f;  // this half's running max and row sum
-    for (int j = 0; j < it.count; ++j, ++g) {
-      TileMeta next = cur;
-      int t_after = 0;
-      if (j + 1 < it.count) next = load_meta(ks_head, p.valid, qs, t_next);
-      if (j + 2 < it.count)
-        t_after = clamp_tile(__ldg(it.idx + j + 2), p.n_tiles);
-      const uint32_t s_addr = lane_addr + tmem_s(g & 1) + 64 * h;
-      const float sc = h ? cur.sc1 : cur.sc0;
-      const float off = h ? cur.off1 : cur.off0;
-
-      good = mbar_wait(&b.s_full[g & 1], (g >> 1) & 1, abort, p.status,
-                       VEDA_STATUS_TIMEOUT);
-      if (!__all_sync(0xffffffffu, good)) {
-        good = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t r[64];
-      tmem_ld32(s_addr + 0, r);
-      tmem_ld32(s_addr + 32, r + 32);
-      tmem_ld_wait(r);
-      reg_fence32(r + 32);
-#pragma unroll
-      for (int c = 0; c < 64; ++c) r[c] += kMagicBits;
-      if (cur.valid < 64 * h + 64) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (64 * h + c >= cur.valid) r[c] = 0xFF800000u;  // -inf, p = 0
-      }
-      float ma = -INFINITY, mb = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 64; c += 4) {
-        ma = max3(ma, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
-        mb = max3(mb, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
-      }
-      const float mt = fmaf(fmaxf(ma, mb), sc, -off);
-      const bool need = mt > m + kRescaleThreshold;
-      float alpha = 1.0f;
-      if (need) {
-        alpha = ex2_approx(m - mt);
-        m = mt;
-        l *= alpha;
-      }
-      const uint64_t s2 = f2(sc, sc);
-      const float cn = -(off + m);
-      const uint64_t n2 = f2(cn, cn);
-      uint64_t acc[4] = {0, 0, 0, 0};
-      uint32_t pk[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const uint64_t z =
-            fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
-                 s2, n2);
-        float z0, z1;
-        f2_split(z, z0, z1);
-        const float p0 = ex2_approx(z0), p1 = ex2_approx(z1);
-        acc[i & 3] = add2(acc[i & 3], f2(p0, p1));
-        pk[i] = Pack<VT>::two(p0, p1);
-      }
-      tmem_st32(s_addr, pk);
-      {
-        float a0, a1, a2, a3, a4, a5, a6, a7;
-        f2_split(acc[0], a0, a1);
-        f2_split(acc[1], a2, a3);
-        f2_split(acc[2], a4, a5);
-        f2_split(acc[3], a6, a7);
-        l += ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
-      }
-      // A grown max rescales O_h, which must first hold this half's P V of
-      // the previous tile (rare after the first tiles of a walk).
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        good = mbar_wait(&b.pv_done[h][(g - 1) & 1], ((g - 1) >> 1) & 1, abort,
-                         p.status, VEDA_STATUS_TIMEOUT);
-        if (!__all_sync(0xffffffffu, good)) {
-          good = false;
-          break;
-        }
-        tc_fence_after();
-        const uint64_t a2v = f2(alpha, alpha);
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t o[32];
-          tmem_ld32(o_self + 32 * cc, o);
-          tmem_ld_wait(o);
-#pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            float x0, x1;
-            f2_split(mul2(f2(__uint_as_float(o[c]), __uint_as_float(o[c + 1])),
-                          a2v), x0, x1);
-            o[c] = __float_as_uint(x0);
-            o[c + 1] = __float_as_uint(x1);
-          }
-          tmem_st32(o_self + 32 * cc, o);
-        }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&b.p_full[h][g & 1]);
-      cur = next;
-      t_next = t_after;
-    }
+    uint32_t r[64];
+    good = sm.wait(&b.s_full[g & 1], (g >> 1) & 1);
+    if (!good) break;
+    tc_fence_after();
+    sm.load_s(g, r);
+    tmem_ld_wait(r);
+    reg_fence32(r + 32);
+    for (int j = 0; j < it.count && good; ++j, ++g) good = sm.step(j, g, r, r);
     if (!good) break;
     // Merge the halves: exchange (m, l), then O = sum_h O_h 2^(m_h - M) /
     // sum_h l_h 2^(m_h - M) for this warpgroup's 64 output columns.
     float2* slot = xch + (n & 1) * 2 * kTile;
-    slot[h * kTile + row] = make_float2(m, l);
+    slot[h * kTile + row] = make_float2(sm.m, sm.l);
     __syncwarp();
     if (lane == 0) mbar_arrive(&b.x_full[n & 1]);
-    good = mbar_wait(&b.x_full[n & 1], (n >> 1) & 1, abort, p.status,
-                     VEDA_STATUS_TIMEOUT) &&
-           mbar_wait(&b.o_ready, n & 1, abort, p.status, VEDA_STATUS_TIMEOUT);
-    if (!__all_sync(0xffffffffu, good)) {
-      good = false;
-      break;
-    }
+    good = sm.wait(&b.x_full[n & 1], (n >> 1) & 1) &&
+           sm.wait(&b.o_ready, n & 1);
+    if (!good) break;
     tc_fence_after();
     const float2 other = slot[(h ^ 1) * kTile + row];
-    const float mx = fmaxf(m, other.x);
-    const float a_self = ex2_approx(m - mx), a_other = ex2_approx(other.x - mx);
-    const float total = l * a_self + other.y * a_other;
+    const float mx = fmaxf(sm.m, other.x);
+    const float a_self = ex2_approx(sm.m - mx), a_other = ex2_approx(other.x - mx);
+    const float total = sm.l * a_self + other.y * a_other;
     const float inv = total > 0.0f ? 1.0f / total : 1.0f;
     const float w_self = a_self * inv, w_other = a_other * inv;
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       uint32_t os[32], oo[32];
-      tmem_ld32(o_self + 64 * h + 32 * cc, os);
+      tmem_ld32(sm.o_self + 64 * h + 32 * cc, os);
       tmem_ld32(o_other + 64 * h + 32 * cc, oo);
       tmem_ld_wait(os);
       reg_fence32(oo);

@@ -71,12 +71,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a phase: the cheap path when it has already completed.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase of `bar` with the given parity to complete. Gives up
 // when another role of the CTA has aborted (`*abort` set) or after
 // kWaitLimitNs; on a timeout it sets `*abort` and reports `code`.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort, int32_t* status,
                                           int32_t code) {
+  if (mbar_test(bar, parity)) return true;
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_ns();
   while (true) {
