@@ -73,11 +73,12 @@ def _round16(p: np.ndarray, kind: str | None) -> np.ndarray:
 
 def int8_block_sparse(q, k, v, index, count, valid_count,
                       softmax_scale=None, p_round: str | None = None,
-                      heads=None):
+                      heads=None, q_tiles=None):
     """INT8 block-sparse attention on tile-ordered [N, H, D] inputs.
 
     index [H, n_tiles, W] ascending kept tile ids, count [H, n_tiles].
     Returns float64 [N, H, D]; query tiles with count 0 give zeros.
+    `heads` / `q_tiles` restrict the work to a sample (other rows stay 0).
     """
     n, n_heads, dim = q.shape
     qi, qs = quantize(q, TILE, q_pre_scale(dim, softmax_scale))
@@ -86,7 +87,7 @@ def int8_block_sparse(q, k, v, index, count, valid_count,
     out = np.zeros((n, n_heads, dim), dtype=np.float64)
     col_in_tile = np.arange(TILE)
     for h in (range(n_heads) if heads is None else heads):
-        for qt in range(n // TILE):
+        for qt in (range(n // TILE) if q_tiles is None else q_tiles):
             c = int(count[h, qt])
             if c == 0:
                 continue

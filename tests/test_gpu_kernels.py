@@ -122,6 +122,8 @@ def test_select_matches_reference_fixture(cuda_device, name):
     rows_equal = (got == want).all(-1)
     assert rows_equal[~ties].all(), np.argwhere(~rows_equal & ~ties)[:8]
     assert int(ties.sum()) == info['boundary_tie_rows']
+    # tie rows keep as many tiles as the reference
+    assert np.array_equal(got.sum(-1), want.sum(-1))
 
 
 def test_mask_to_index_matches_oracle(cuda_device):

@@ -64,7 +64,8 @@ class VedaAttention:
               layout, *, scores: torch.Tensor | None = None,
               proj_q: torch.Tensor | None = None,
               proj_k: torch.Tensor | None = None, full: bool = False,
-              out: torch.Tensor | None = None) -> torch.Tensor:
+              out: torch.Tensor | None = None,
+              tiled: bool | None = None) -> torch.Tensor:
         """Veda attention of one layer.
 
         Args:
@@ -75,12 +76,19 @@ class VedaAttention:
                 computed from `proj_q` / `proj_k` ([H, 384, 128]).
             full: Full attention (every non-empty key tile).
             out: Optional output [S or N, H, 128].
+            tiled: Whether q / k / v are already in tile order. By default
+                they are when they have N rows and either the layout is the
+                identity or N differs from the packed length S.
 
         Returns:
-            Attention output with q's leading shape and v's dtype.
+            Attention output with q's leading shape and v's dtype, in the
+            order of the inputs (tile order for tiled inputs).
         """
         heads = q.shape[1]
-        tiled_in = q.shape[0] == layout.num_slots and layout.identity
+        if tiled is None:
+            tiled = q.shape[0] == layout.num_slots and (
+                layout.identity or q.shape[0] != layout.seq_len)
+        tiled_in = tiled
         head_ids = None
         if tiled_in:
             q_t, k_t, v_t = q, k, v

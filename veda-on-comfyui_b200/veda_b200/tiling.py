@@ -158,6 +158,19 @@ def identity_layout(real_tokens: int,
     return _layout(perm, n_tiles, 0, 0, 0, real_tokens, real_tokens, device)
 
 
+def from_reference(layout, device: torch.device | str | None = None
+                   ) -> TileLayout:
+    """This package's TileLayout from the reference's own (core/tiling.py:
+    115-168): the same permutation and tile counts; the reference's derived
+    index tensors (gather_index, scatter_index, ...) are not needed here.
+    Reads `perm` once on the host, so convert once per geometry."""
+    perm = layout.perm.detach().to('cpu', torch.int64).numpy()
+    device = layout.perm.device if device is None else device
+    return _layout(perm, int(layout.n_video_tiles), int(layout.n_ref_tiles),
+                   int(layout.n_global_tiles), int(layout.ref_tokens),
+                   int(layout.target_tokens), int(layout.seq_len), device)
+
+
 def gather_tiles(x: torch.Tensor, layout, heads: torch.Tensor) -> torch.Tensor:
     """[S, H, D] packed -> [N, H', D] contiguous tile order, padding zero."""
     return ops.gather_tiles(x, layout.perm, heads)
