@@ -100,6 +100,27 @@ int veda_tile_logits(const float* feats_q, const float* feats_k,
                      int heads, int n_q, int n_k, float* workspace,
                      float* logits, void* stream);
 
+/* Row limit of veda_tile_logits_static: (n_q + n_k) * heads. */
+#define VEDA_STATIC_LOGITS_ROWS 16384
+
+/*
+ * veda_tile_logits that allocates nothing: its scratch (the projected
+ * features) is a fixed 8 MiB device array inside this library, one per
+ * device, instead of a caller workspace. This entry point has no
+ * counterpart in the reference, whose predictor allocates through torch.
+ *   Limit: (n_q + n_k) * heads <= VEDA_STATIC_LOGITS_ROWS; larger calls
+ *   return VEDA_ERR_INVALID before any work.
+ *   Calls that overlap in time on one device (other streams or threads)
+ *   share the array and race: serialise them.
+ *   The first call on each device looks up the array's address (with that
+ *   device current); make it before any stream capture.
+ * Arguments and results are those of veda_tile_logits.
+ */
+int veda_tile_logits_static(const float* feats_q, const float* feats_k,
+                            const void* proj_q, const void* proj_k,
+                            int proj_dtype, int heads, int n_q, int n_k,
+                            float* logits, void* stream);
+
 /* One sparse column block of the video quadrant
  * (core/selection.py:109-128 ColumnBlock / column_blocks). */
 typedef struct veda_column_block {

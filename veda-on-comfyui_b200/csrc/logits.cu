@@ -4,6 +4,8 @@
 // fp32 on CUDA cores: about 1.2 GFLOP for 24 heads x 256 tiles, far below
 // anything worth a tensor-core pipeline, and fp32 keeps the logits (and so
 // the selection) within rounding of the reference's fp32 bmm.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace veda {
@@ -97,24 +99,54 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-}  // namespace
-}  // namespace veda
+// Scratch of veda_tile_logits_static: the projected features (q_hat, k_hat)
+// of at most VEDA_STATIC_LOGITS_ROWS rows, 8 MiB in every device context
+// that loads this library. Nothing in it needs to start at zero: each call's
+// projection writes every element its logits then read.
+static __device__ __align__(256) float g_static_logits_scratch[
+    static_cast<int64_t>(VEDA_STATIC_LOGITS_ROWS) * kDim];
 
-using namespace veda;
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mutex;
+float* g_static_scratch[kMaxDevices] = {};
 
-extern "C" int veda_tile_logits(const float* feats_q, const float* feats_k,
-                                const void* proj_q, const void* proj_k,
-                                int proj_dtype, int heads, int n_q, int n_k,
-                                float* workspace, float* logits,
-                                void* stream) {
-  if (int rc = check_device()) return rc;
+// Address of the scratch on the current device, looked up once per device
+// (with that device current, as cudaGetSymbolAddress requires).
+int static_scratch(float** out) {
+  int device = 0;
+  VEDA_CHECK_CUDA(cudaGetDevice(&device));
+  if (device < 0 || device >= kMaxDevices)
+    return fail(VEDA_ERR_UNSUPPORTED, "device %d is past the %d this library "
+                "tracks", device, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (g_static_scratch[device] == nullptr) {
+    void* address = nullptr;
+    const cudaError_t err =
+        cudaGetSymbolAddress(&address, g_static_logits_scratch);
+    if (err != cudaSuccess)
+      return cuda_fail(err, "cudaGetSymbolAddress(static logits scratch)");
+    g_static_scratch[device] = static_cast<float*>(address);
+  }
+  *out = g_static_scratch[device];
+  return VEDA_OK;
+}
+
+int check_logits_args(const float* feats_q, const float* feats_k,
+                      const void* proj_q, const void* proj_k, int heads,
+                      int n_q, int n_k, const float* logits) {
   if (heads <= 0 || heads > 65535 || n_q <= 0 || n_k <= 0)
     return fail(VEDA_ERR_INVALID, "bad sizes: heads %d, n_q %d, n_k %d", heads,
                 n_q, n_k);
   if (feats_q == nullptr || feats_k == nullptr || proj_q == nullptr ||
-      proj_k == nullptr || workspace == nullptr || logits == nullptr)
+      proj_k == nullptr || logits == nullptr)
     return fail(VEDA_ERR_INVALID, "null pointer argument");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return VEDA_OK;
+}
+
+int launch_tile_logits(const float* feats_q, const float* feats_k,
+                       const void* proj_q, const void* proj_k, int proj_dtype,
+                       int heads, int n_q, int n_k, float* workspace,
+                       float* logits, cudaStream_t s) {
   float* hat_q = workspace;
   float* hat_k = workspace + static_cast<int64_t>(heads) * n_q * kDim;
   const int n_max = n_q > n_k ? n_q : n_k;
@@ -144,4 +176,46 @@ extern "C" int veda_tile_logits(const float* feats_q, const float* feats_k,
   logits_kernel<<<lgrid, 256, 0, s>>>(hat_q, hat_k, n_q, n_k, logits);
   VEDA_CHECK_CUDA(cudaGetLastError());
   return VEDA_OK;
+}
+
+}  // namespace
+}  // namespace veda
+
+using namespace veda;
+
+extern "C" int veda_tile_logits(const float* feats_q, const float* feats_k,
+                                const void* proj_q, const void* proj_k,
+                                int proj_dtype, int heads, int n_q, int n_k,
+                                float* workspace, float* logits,
+                                void* stream) {
+  if (int rc = check_device()) return rc;
+  if (int rc = check_logits_args(feats_q, feats_k, proj_q, proj_k, heads, n_q,
+                                 n_k, logits))
+    return rc;
+  if (workspace == nullptr) return fail(VEDA_ERR_INVALID, "null workspace");
+  return launch_tile_logits(feats_q, feats_k, proj_q, proj_k, proj_dtype,
+                            heads, n_q, n_k, workspace, logits,
+                            static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int veda_tile_logits_static(const float* feats_q,
+                                       const float* feats_k,
+                                       const void* proj_q, const void* proj_k,
+                                       int proj_dtype, int heads, int n_q,
+                                       int n_k, float* logits, void* stream) {
+  if (int rc = check_device()) return rc;
+  if (int rc = check_logits_args(feats_q, feats_k, proj_q, proj_k, heads, n_q,
+                                 n_k, logits))
+    return rc;
+  const int64_t rows = static_cast<int64_t>(n_q + n_k) * heads;
+  if (rows > VEDA_STATIC_LOGITS_ROWS)
+    return fail(VEDA_ERR_INVALID,
+                "(n_q + n_k) * heads = %lld rows exceeds the static scratch "
+                "limit of %d rows; use veda_tile_logits with a workspace",
+                static_cast<long long>(rows), VEDA_STATIC_LOGITS_ROWS);
+  float* scratch = nullptr;
+  if (int rc = static_scratch(&scratch)) return rc;
+  return launch_tile_logits(feats_q, feats_k, proj_q, proj_k, proj_dtype,
+                            heads, n_q, n_k, scratch, logits,
+                            static_cast<cudaStream_t>(stream));
 }

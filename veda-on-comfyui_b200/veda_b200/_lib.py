@@ -66,6 +66,7 @@ SIGNATURES = {
     'veda_quant_pool': [_P, _P, _I, _L, _L, _I, _I, _P, _I, _F, _P, _P, _P,
                         _P, _P, _P, _P],
     'veda_tile_logits': [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P],
+    'veda_tile_logits_static': [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P],
     'veda_select': [_P, _L, _L, _I, _I, _I, _P, _I,
                     ctypes.POINTER(ColumnBlock), _P, _I, _P, _P, _P, _P],
     'veda_mask_to_index': [_P, _P, _I, _I, _I, _P, _P, _P, _P],
