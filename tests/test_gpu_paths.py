@@ -78,15 +78,12 @@ def test_cfg1_call_matches_oracle(cuda_device):
     assert np.array_equal(count, ocnt)
     assert np.array_equal(helpers.lists_to_mask(index, count, 256),
                           helpers.lists_to_mask(oidx, ocnt, 256))
-    # int8 codes and scales of sampled tiles
-    qi, qs = kernels.quantize(dq, 128, 128 ** -0.5 * kernels.LOG2E)
-    oqi, oqs = oint8.quantize(qkv[0].float().numpy(), 128,
-                              oint8.q_pre_scale(128))
-    qi, qs = qi.cpu().numpy(), qs.cpu().numpy()
-    for h, t in [(0, 0), (5, 100), (23, 255), (17, 3)]:
-        rows = slice(t * 128, (t + 1) * 128)
-        assert np.array_equal(qi[h, rows], oqi[rows, h])
-        assert qs[h, t] == oqs[h, t]
+    # every int8 code and scale of Q (128-row blocks) and K (64-row blocks)
+    for x, block, pre in [(0, 128, oint8.q_pre_scale(128)), (1, 64, 1.0)]:
+        qi, qs = kernels.quantize(dq if x == 0 else dk, block, float(pre))
+        oqi, oqs = oint8.quantize(qkv[x].float().numpy(), block, pre)
+        assert np.array_equal(qi.cpu().numpy(), oqi.transpose(1, 0, 2))
+        assert np.array_equal(qs.cpu().numpy(), oqs)
     _check_sampled(_np(out), qkv, index, count, olayout.valid_count,
                    [0, 11, 23], [0, 97, 255], olayout.slot_valid.astype(bool))
 

@@ -311,14 +311,6 @@ __device__ void store_row(VT* dst, const float* v) {
   }
 }
 
-// Per-tile constants of the softmax: the two K-half scales folded with the
-// Q scale, the magic-number offsets that go with them, the valid rows.
-struct TileMeta {
-  float sc0, sc1;    // q_scale * k_scale of key rows 0-63 / 64-127
-  float off0, off1;  // 1.5 * 2^23 * sc0 / sc1
-  int valid;
-};
-
 // int32 S + 0x4B400000, read as fp32, is exactly 1.5 * 2^23 + S for
 // |S| < 2^22 (|S| <= 128 * 127 * 127 here), so S * sc - m comes out of one
 // fused multiply-add on the biased value: (1.5 * 2^23 + S) * sc - (off + m).
@@ -327,19 +319,6 @@ struct TileMeta {
 // INT8 quantisation itself puts into S.
 constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-
-__device__ __forceinline__ TileMeta load_meta(const float* ks_head,
-                                              const int32_t* valid, float qs,
-                                              int t) {
-  const float2 ks = __ldg(reinterpret_cast<const float2*>(ks_head + 2 * t));
-  TileMeta m;
-  m.sc0 = qs * ks.x;
-  m.sc1 = qs * ks.y;
-  m.off0 = kMagic * m.sc0;
-  m.off1 = kMagic * m.sc1;
-  m.valid = __ldg(valid + t);
-  return m;
-}
 
 // Warps 4-7 (key half 0) and 8-11 (key half 1): the softmax of one half of
 // every tile of every item, one row per thread; at the end of each walk the

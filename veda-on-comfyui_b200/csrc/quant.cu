@@ -4,8 +4,8 @@
 // Arithmetic of kernels/sage/sparse_int8.py:57-73 (reference): x * pre_scale
 // in fp32; scale = max|x| / 127 per (block, head), 1 for an all-zero block;
 // q = x / scale; q += 0.5 * sign (>= 0 counts as positive); int8 = trunc(q).
-// IEEE-rounded division (__fdiv_rn), so the int8 codes are bit-exact with an
-// fp32 restatement of those steps.
+// The quotient is the IEEE-rounded one (see quant_one), so the int8 codes
+// are bit-exact with an fp32 restatement of those steps.
 //
 // Pooling follows core/predictor.py:20-60: mean (fp32 sum / max(valid, 1)),
 // max and min over the real rows of each video tile, all 0 for an empty tile.
@@ -57,8 +57,16 @@ __device__ __forceinline__ void load8(const __half* p, float* f) {
   }
 }
 
-__device__ __forceinline__ int8_t quant_one(float x, float scale) {
-  float q = __fdiv_rn(x, scale);
+// x / b rounded to nearest, without a division per element: with
+// y = RN(1 / b), q0 = RN(x y) is within one ulp of x / b, the residual
+// r = x - b q0 is exact in one FMA, and RN(q0 + r y) = RN(x / b)
+// (Markstein's theorem on FMA-corrected division). Only quotients of tiny
+// magnitude (subnormal residuals) can differ, and those quantise to 0
+// either way; the codes are those of an IEEE division.
+__device__ __forceinline__ int8_t quant_one(float x, float b, float y) {
+  const float q0 = __fmul_rn(x, y);
+  const float r = __fmaf_rn(-q0, b, x);
+  float q = __fmaf_rn(r, y, q0);
   q = __fadd_rn(q, q >= 0.0f ? 0.5f : -0.5f);
   return static_cast<int8_t>(__float2int_rz(q));
 }
@@ -68,7 +76,7 @@ __global__ void __launch_bounds__(kQuantThreads)
     quant_pool_kernel(const QuantParams p) {
   __shared__ float amax_sh[8][2];
   __shared__ float pool_sh[8][3][kDim];
-  __shared__ float scale_sh[2];
+  __shared__ float scale_sh[2], inv_sh[2];
 
   const QuantJob job = blockIdx.z == 0 ? p.job[0] : p.job[1];
   const int tile = blockIdx.x, head = blockIdx.y;
@@ -154,7 +162,9 @@ __global__ void __launch_bounds__(kQuantThreads)
     float m = tid == 0 ? m0 : m1;
     if (job.block == kTile) m = fmaxf(m0, m1);
     float sc = __fdiv_rn(m, 127.0f);
-    scale_sh[tid] = sc > 0.0f ? sc : 1.0f;
+    sc = sc > 0.0f ? sc : 1.0f;
+    scale_sh[tid] = sc;
+    inv_sh[tid] = __frcp_rn(sc);
   }
   if (pool && tid < kDim) {
     float s = 0.0f, mx = -INFINITY, mn = INFINITY;
@@ -173,17 +183,18 @@ __global__ void __launch_bounds__(kQuantThreads)
   __syncthreads();
 
   const float sc[2] = {scale_sh[0], scale_sh[1]};
+  const float inv[2] = {inv_sh[0], inv_sh[1]};
   const int64_t n_slots = static_cast<int64_t>(p.n_tiles) * kTile;
   int8_t* out = job.out + (static_cast<int64_t>(head) * n_slots +
                            static_cast<int64_t>(tile) * kTile) * kDim + 8 * dc;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float s = sc[i >> 2];
+    const float s = sc[i >> 2], y = inv[i >> 2];
     uint32_t lo = 0, hi = 0;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      lo |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one(v[i][e], s))) << (8 * e);
-      hi |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one(v[i][e + 4], s))) << (8 * e);
+      lo |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one(v[i][e], s, y))) << (8 * e);
+      hi |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one(v[i][e + 4], s, y))) << (8 * e);
     }
     *reinterpret_cast<uint2*>(out + (rg + 16 * i) * kDim) = make_uint2(lo, hi);
   }
