@@ -36,8 +36,9 @@ struct QuantParams {
   int n_video;
 };
 
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* f) {
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+// Eight 16-bit values of one 16-byte load, widened to fp32 (exact).
+__device__ __forceinline__ void unpack8(const uint4& u, float* f,
+                                        __nv_bfloat16) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -46,8 +47,7 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* f) {
   }
 }
 
-__device__ __forceinline__ void load8(const __half* p, float* f) {
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+__device__ __forceinline__ void unpack8(const uint4& u, float* f, __half) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -71,11 +71,14 @@ __device__ __forceinline__ int8_t quant_one(float x, float b, float y) {
   return static_cast<int8_t>(__float2int_rz(q));
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kQuantThreads)
+// The tile is held as raw 16-bit words (32 registers a thread) and widened
+// twice, once for the block max and once for the codes, so three CTAs fit
+// on an SM and more loads are in flight. POOL adds the TripPool features.
+template <typename T, bool POOL>
+__global__ void __launch_bounds__(kQuantThreads, POOL ? 2 : 3)
     quant_pool_kernel(const QuantParams p) {
   __shared__ float amax_sh[8][2];
-  __shared__ float pool_sh[8][3][kDim];
+  __shared__ float pool_sh[POOL ? 8 : 1][3][kDim];
   __shared__ float scale_sh[2], inv_sh[2];
 
   const QuantJob job = blockIdx.z == 0 ? p.job[0] : p.job[1];
@@ -83,36 +86,47 @@ __global__ void __launch_bounds__(kQuantThreads)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int dc = tid & 15;  // dims 8*dc .. 8*dc+7
   const int rg = tid >> 4;  // rows rg + 16 i
-  const int valid = p.valid != nullptr ? __ldg(p.valid + tile) : kTile;
 
   const T* x = static_cast<const T*>(job.x) +
                static_cast<int64_t>(tile) * kTile * p.stride_n +
                static_cast<int64_t>(head) * p.stride_h + 8 * dc;
-  float v[8][8];
+  uint4 raw[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) load8(x + (rg + 16 * i) * p.stride_n, v[i]);
+  for (int i = 0; i < 8; ++i)
+    raw[i] = __ldg(reinterpret_cast<const uint4*>(x + (rg + 16 * i) * p.stride_n));
+  const float pre = job.pre_scale;
 
-  // TripPool over the real rows (a prefix of the tile), before pre-scaling.
-  const bool pool = job.feats != nullptr && tile < p.n_video;
-  if (pool) {
-    float s[8], mx[8], mn[8];
+  // TripPool over the real rows (a prefix of the tile), before pre-scaling,
+  // and max |x * pre| of rows 0-63 (a[0]) and 64-127 (a[1]).
+  const bool pool = POOL && job.feats != nullptr && tile < p.n_video;
+  const int valid = POOL && p.valid != nullptr ? __ldg(p.valid + tile) : kTile;
+  float s[8], mx[8], mn[8];
+  if (POOL) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       s[e] = 0.0f;
       mx[e] = -INFINITY;
       mn[e] = INFINITY;
     }
+  }
+  float a[2] = {0.0f, 0.0f};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (rg + 16 * i < valid) {
+  for (int i = 0; i < 8; ++i) {
+    float f[8];
+    unpack8(raw[i], f, T());
+    if (POOL && pool && rg + 16 * i < valid) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          s[e] += v[i][e];
-          mx[e] = fmaxf(mx[e], v[i][e]);
-          mn[e] = fminf(mn[e], v[i][e]);
-        }
+      for (int e = 0; e < 8; ++e) {
+        s[e] += f[e];
+        mx[e] = fmaxf(mx[e], f[e]);
+        mn[e] = fminf(mn[e], f[e]);
       }
     }
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      a[i >> 2] = fmaxf(a[i >> 2], fabsf(__fmul_rn(f[e], pre)));
+  }
+  if (POOL && pool) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       s[e] += __shfl_xor_sync(0xffffffffu, s[e], 16);
@@ -128,20 +142,6 @@ __global__ void __launch_bounds__(kQuantThreads)
       }
     }
   }
-
-  if (job.pre_scale != 1.0f) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[i][e] = __fmul_rn(v[i][e], job.pre_scale);
-  }
-
-  // max |x| of rows 0-63 (a[0]) and 64-127 (a[1]).
-  float a[2] = {0.0f, 0.0f};
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) a[i >> 2] = fmaxf(a[i >> 2], fabsf(v[i][e]));
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
     a[0] = fmaxf(a[0], __shfl_xor_sync(0xffffffffu, a[0], off));
@@ -166,19 +166,19 @@ __global__ void __launch_bounds__(kQuantThreads)
     scale_sh[tid] = sc;
     inv_sh[tid] = __frcp_rn(sc);
   }
-  if (pool && tid < kDim) {
-    float s = 0.0f, mx = -INFINITY, mn = INFINITY;
+  if (POOL && pool && tid < kDim) {
+    float sum = 0.0f, hi = -INFINITY, lo = INFINITY;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
-      s += pool_sh[w][0][tid];
-      mx = fmaxf(mx, pool_sh[w][1][tid]);
-      mn = fminf(mn, pool_sh[w][2][tid]);
+      sum += pool_sh[w][0][tid];
+      hi = fmaxf(hi, pool_sh[w][1][tid]);
+      lo = fminf(lo, pool_sh[w][2][tid]);
     }
     float* f = job.feats + (static_cast<int64_t>(head) * p.n_video + tile) * 3 * kDim;
     const bool live = valid > 0;
-    f[tid] = live ? __fdiv_rn(s, static_cast<float>(valid)) : 0.0f;
-    f[kDim + tid] = live ? mx : 0.0f;
-    f[2 * kDim + tid] = live ? mn : 0.0f;
+    f[tid] = live ? __fdiv_rn(sum, static_cast<float>(valid)) : 0.0f;
+    f[kDim + tid] = live ? hi : 0.0f;
+    f[2 * kDim + tid] = live ? lo : 0.0f;
   }
   __syncthreads();
 
@@ -189,12 +189,16 @@ __global__ void __launch_bounds__(kQuantThreads)
                            static_cast<int64_t>(tile) * kTile) * kDim + 8 * dc;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float s = sc[i >> 2], y = inv[i >> 2];
+    const float b = sc[i >> 2], y = inv[i >> 2];
+    float f[8];
+    unpack8(raw[i], f, T());
     uint32_t lo = 0, hi = 0;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      lo |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one(v[i][e], s, y))) << (8 * e);
-      hi |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one(v[i][e + 4], s, y))) << (8 * e);
+      lo |= static_cast<uint32_t>(static_cast<uint8_t>(
+                quant_one(__fmul_rn(f[e], pre), b, y))) << (8 * e);
+      hi |= static_cast<uint32_t>(static_cast<uint8_t>(
+                quant_one(__fmul_rn(f[e + 4], pre), b, y))) << (8 * e);
     }
     *reinterpret_cast<uint2*>(out + (rg + 16 * i) * kDim) = make_uint2(lo, hi);
   }
@@ -202,9 +206,9 @@ __global__ void __launch_bounds__(kQuantThreads)
     if (job.block == kTile) {
       job.scale[static_cast<int64_t>(head) * p.n_tiles + tile] = sc[0];
     } else {
-      float* s = job.scale + static_cast<int64_t>(head) * 2 * p.n_tiles + 2 * tile;
-      s[0] = sc[0];
-      s[1] = sc[1];
+      float* sp = job.scale + static_cast<int64_t>(head) * 2 * p.n_tiles + 2 * tile;
+      sp[0] = sc[0];
+      sp[1] = sc[1];
     }
   }
 }
@@ -212,10 +216,18 @@ __global__ void __launch_bounds__(kQuantThreads)
 int launch_quant(const QuantParams& p, int n_jobs, int heads, int dtype,
                  cudaStream_t stream) {
   dim3 grid(p.n_tiles, heads, n_jobs);
-  if (dtype == VEDA_BF16)
-    quant_pool_kernel<__nv_bfloat16><<<grid, kQuantThreads, 0, stream>>>(p);
-  else
-    quant_pool_kernel<__half><<<grid, kQuantThreads, 0, stream>>>(p);
+  const bool pool = p.job[0].feats != nullptr && p.n_video > 0;
+  if (dtype == VEDA_BF16) {
+    if (pool)
+      quant_pool_kernel<__nv_bfloat16, true><<<grid, kQuantThreads, 0, stream>>>(p);
+    else
+      quant_pool_kernel<__nv_bfloat16, false><<<grid, kQuantThreads, 0, stream>>>(p);
+  } else {
+    if (pool)
+      quant_pool_kernel<__half, true><<<grid, kQuantThreads, 0, stream>>>(p);
+    else
+      quant_pool_kernel<__half, false><<<grid, kQuantThreads, 0, stream>>>(p);
+  }
   VEDA_CHECK_CUDA(cudaGetLastError());
   return VEDA_OK;
 }
