@@ -6,32 +6,30 @@
 // folded in, so these are base-2 logits); key columns at or past the tile's
 // valid count are masked; online softmax with exp2; O += P V; out = O / l.
 //
-// B200 mapping: a persistent CTA per SM (384 threads, ~177 KB of shared
-// memory, all 512 TMEM columns) walks query tiles ("items") one after the
-// other. Within a walk the key tiles g are double-buffered in TMEM, so the
-// tensor core computes S of tile g + 2 while the softmax works on tile
-// g + 1, and each key tile is split into its two 64-key halves, each with
-// its own softmax warpgroup, running max, row sum and O accumulator (the
-// split-KV form of the online softmax); the halves are merged once per
-// walk, O = sum_h O_h 2^(m_h - M) / sum_h l_h 2^(m_h - M), M = max_h m_h.
-//   warp 0       TMA producer: the item's Q tile (int8, double buffered
-//                across items), then K (int8, 16 KB) and V (16-bit, 32 KB)
-//                of each listed key tile into a 3-stage ring, 128-byte
-//                swizzled, fetched by tile id.
-//   warp 1       P V issuer (and TMEM allocator): O_h(TMEM, f32) (+)=
-//                P_h(TMEM) V_h(smem) as 4 x tcgen05.mma kind::f16 (K = 16)
-//                per key half h.
-//   warp 2       Q K^T issuer: S(TMEM, s32) = Q K^T as 4 x kind::i8
-//                (K = 32), once the P V that read the same S buffer is done.
-//   warps 4-7    softmax of key half 0, warps 8-11 of key half 1: one query
-//                row per thread (TMEM lane = row); load the half row of S,
-//                scale, mask, running max with lazy rescaling of O_h (only
-//                when the max grows by > 2^8), exp2, write P_h as packed
-//                16-bit pairs over the first 32 columns of the half; at the
-//                end of a walk, merge the halves and store the row.
-// TMEM: S0 [0, 128), S1 [128, 256), O_0 [256, 384), O_1 [384, 512);
-// P_h aliases columns [64h, 64h + 32) of S. Every wait is bounded
-// (VEDA_STATUS_TIMEOUT) and ends the CTA cleanly.
+// B200 mapping: a persistent CTA per SM (384 threads, 208 KB of shared
+// memory, all 512 TMEM columns) walks pairs of query tiles of one head, the
+// two tiles ("slots" A and B) each with its own key-tile list:
+//   warp 0       TMA producer: per pair the two Q tiles (int8, double
+//                buffered across pairs), then K (int8, 16 KB) and V
+//                (16-bit, 32 KB) of each listed key tile, A and B
+//                interleaved, into a 3-stage ring, 128-byte swizzled.
+//   warp 1       TMEM allocator and the single MMA-issuing thread, in the
+//                fixed order P_A V -> Q_A K' -> P_B V -> Q_B K' ...:
+//                S(TMEM, s32) = Q K^T as 4 x tcgen05.mma kind::i8 (K = 32),
+//                O(TMEM, f32) += P(TMEM) V(smem) as 8 x kind::f16 (K = 16).
+//                While one slot's softmax runs, the tensor core serves the
+//                other slot, so exp and MMA overlap.
+//   warps 4-7    softmax of slot A, warps 8-11 of slot B: one query row per
+//                thread (TMEM lane = row); load the S row, scale, mask,
+//                running max with lazy rescaling of O (only when the max
+//                grows by > 2^8), exp2, write P as packed 16-bit pairs over
+//                the first 64 columns of S; at the end of a tile's walk,
+//                normalise O and store the rows.
+// TMEM: S_A [0, 128), S_B [128, 256), O_A [256, 384), O_B [384, 512); P
+// aliases S. One thread issues every MMA and the tensor pipe runs them in
+// order, so a Q K^T cannot overwrite P before the P V that reads it, and a
+// commit after a Q K^T also covers the P V before it (O is complete
+// whenever S is ready). Every wait is bounded (VEDA_STATUS_TIMEOUT).
 #include <atomic>
 
 #include "common.cuh"
@@ -40,36 +38,38 @@ namespace veda {
 namespace {
 
 constexpr int kAttnThreads = 384;
+constexpr int kSlots = 2;
 constexpr int kStages = 3;
 constexpr uint32_t kQBytes = kTile * kDim;      // int8 Q tile
 constexpr uint32_t kKBytes = kTile * kDim;      // int8 K tile
 constexpr uint32_t kVBytes = kTile * kDim * 2;  // 16-bit V tile
-constexpr uint32_t kSmemQ = 0;                  // 2 Q buffers
-constexpr uint32_t kSmemK = kSmemQ + 2 * kQBytes;
+constexpr uint32_t kSmemQ = 0;                  // [slot][buffer] Q tiles
+constexpr uint32_t kSmemK = kSmemQ + 4 * kQBytes;
 constexpr uint32_t kSmemV = kSmemK + kStages * kKBytes;
-constexpr uint32_t kSmemXch = kSmemV + kStages * kVBytes;  // [2][2][128] float2
-constexpr uint32_t kSmemBar = kSmemXch + 2 * 2 * kTile * 8;
+constexpr uint32_t kSmemBar = kSmemV + kStages * kVBytes;
 constexpr uint32_t kSmemBytes = kSmemBar + 512;
 constexpr uint32_t kTmemCols = 512;
 // O is rescaled only when a row's max grows by more than this (log2 units),
 // so P stays below 2^8 and the final O / l is unchanged.
 constexpr float kRescaleThreshold = 8.0f;
-// Register split (setmaxnreg) of the 384 x 168 registers the CTA launches
-// with: producer / issuers 128 x 80, softmax 256 x 200 (61440 in all).
-constexpr uint32_t kIssueRegs = 80;
-constexpr uint32_t kSoftmaxRegs = 200;
+// Register split (setmaxnreg): the producer / MMA warpgroup gives up
+// registers to the two softmax warpgroups. 384 threads launch with 168
+// each (64512); 128 x 64 + 256 x 216 = 63488 stays within that.
+constexpr uint32_t kLowRegs = 64;
+constexpr uint32_t kHighRegs = 216;
 
-__host__ __device__ constexpr uint32_t tmem_s(int b) { return 128u * b; }
-__host__ __device__ constexpr uint32_t tmem_o(int h) { return 256u + 128u * h; }
+__host__ __device__ constexpr uint32_t tmem_s(int slot) { return 128u * slot; }
+__host__ __device__ constexpr uint32_t tmem_o(int slot) {
+  return 256u + 128u * slot;
+}
 
 struct Barriers {
-  uint64_t q_full[2], q_empty[2];
+  uint64_t q_full[kSlots][2], q_empty[kSlots][2];
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t p_full[2][2], pv_done[2][2];  // [key half][S buffer]
-  uint64_t o_ready, x_full[2], o_free;
-  uint64_t fin[2];
+  uint64_t s_full[kSlots], p_full[kSlots];
+  uint64_t o_ready[kSlots], o_free[kSlots];
+  uint64_t fin;
   uint32_t tmem_base;
   int abort;
 };
@@ -84,7 +84,7 @@ struct AttnParams {
   void* out;
   int64_t out_sn, out_sh;
   int n_tiles, width, heads;
-  int n_items;           // heads * n_tiles
+  int n_pairs;           // heads * ceil(n_tiles / 2)
   int32_t* status;
 };
 
@@ -107,6 +107,39 @@ struct Pack<__half> {
   }
 };
 
+// A pair of query tiles of one head; slot B is absent (qt >= n_tiles) for
+// the last pair of a head with an odd tile count.
+struct Pair {
+  int head;
+  int qt[kSlots];
+  int count[kSlots];       // kept key tiles, 0 when the slot is absent
+  const int32_t* idx[kSlots];
+};
+
+__device__ __forceinline__ Pair decode_pair(int w, const AttnParams& p) {
+  const int per_head = (p.n_tiles + 1) >> 1;
+  Pair pr;
+  pr.head = w / per_head;
+  const int first = 2 * (w - pr.head * per_head);
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s) {
+    const int qt = first + s;
+    pr.qt[s] = qt;
+    pr.count[s] = 0;
+    pr.idx[s] = nullptr;
+    if (qt < p.n_tiles) {
+      const int64_t row = static_cast<int64_t>(pr.head) * p.n_tiles + qt;
+      int c = __ldg(p.count + row);
+      if (c < 0 || c > p.width) {
+        if (threadIdx.x == 0) report(p.status, VEDA_STATUS_BAD_COUNT);
+        c = c < 0 ? 0 : p.width;
+      }
+      pr.count[s] = c;
+      pr.idx[s] = p.index + row * p.width;
+    }
+  }
+  return pr;
+}
 
 // Bounded wait that ignores the abort flag: used to drain copies and MMAs
 // this CTA issued before it exits.
@@ -126,34 +159,13 @@ __device__ __forceinline__ int clamp_tile(int t, int n_tiles) {
   return (t < 0 || t >= n_tiles) ? 0 : t;
 }
 
-// One query tile of one head and its key-tile list.
-struct Item {
-  int head, qt, count;
-  const int32_t* idx;
-};
-
-__device__ __forceinline__ Item decode_item(int w, const AttnParams& p) {
-  Item it;
-  it.head = w / p.n_tiles;
-  it.qt = w - it.head * p.n_tiles;
-  const int64_t row = static_cast<int64_t>(it.head) * p.n_tiles + it.qt;
-  int c = __ldg(p.count + row);
-  if (c < 0 || c > p.width) {
-    if (threadIdx.x == 0) report(p.status, VEDA_STATUS_BAD_COUNT);
-    c = c < 0 ? 0 : p.width;
-  }
-  it.count = c;
-  it.idx = p.index + row * p.width;
-  return it;
+__device__ __forceinline__ uint8_t* q_tile(uint8_t* smem, int slot, int buf) {
+  return smem + kSmemQ + (2 * slot + buf) * kQBytes;
 }
 
-// Items with a non-empty list are numbered n = 0, 1, ... by every role in
-// the same order; tiles of those lists are numbered g = 0, 1, ... across
-// items. Item n uses Q buffer n % 2; tile g uses S buffer g % 2 and ring
-// stage g % 3.
-
-// Warp 0, one thread: the Q tile of each item, then its K / V tiles.
-__device__ __forceinline__ void produce(const CUtensorMap* qm, const CUtensorMap* km,
+// Warp 0, one thread: Q tiles per pair, then K / V tiles in the order the
+// MMA thread consumes them (A and B interleaved, tile by tile).
+__device__ void produce(const CUtensorMap* qm, const CUtensorMap* km,
                         const CUtensorMap* vm, uint8_t* smem, Barriers& b,
                         const AttnParams& p) {
   volatile int* abort = &b.abort;
@@ -161,141 +173,153 @@ __device__ __forceinline__ void produce(const CUtensorMap* qm, const CUtensorMap
   tma_prefetch(km);
   tma_prefetch(vm);
   const int n_slots = p.n_tiles * kTile;
-  int n = 0, gk = 0, gv = 0;
+  int q_uses[kSlots][2] = {{0, 0}, {0, 0}};
+  int gk = 0, gv = 0;  // K / V tiles issued (ring positions)
   bool ok = true;
-  for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
-    const Item it = decode_item(w, p);
-    if (it.count == 0) continue;
-    ok = mbar_wait(&b.q_empty[n & 1], ((n >> 1) & 1) ^ 1, abort, p.status,
-                   VEDA_STATUS_TIMEOUT);
-    if (!ok) break;
-    mbar_expect_tx(&b.q_full[n & 1], kQBytes);
-    tma_load_2d(qm, smem + kSmemQ + (n & 1) * kQBytes, &b.q_full[n & 1], 0,
-                it.head * n_slots + it.qt * kTile);
-    ++n;
-    int t_raw = __ldg(it.idx);
-    for (int j = 0; j < it.count && ok; ++j) {
-      int t = t_raw;
-      if (j + 1 < it.count) t_raw = __ldg(it.idx + j + 1);  // used next step
-      if (t < 0 || t >= p.n_tiles) report(p.status, VEDA_STATUS_BAD_INDEX);
-      t = clamp_tile(t, p.n_tiles);
-      const int stage = gk % kStages;
-      const uint32_t ph = (gk / kStages) & 1;
-      ok = mbar_wait(&b.k_empty[stage], ph ^ 1, abort, p.status,
-                     VEDA_STATUS_TIMEOUT);
+  int it = 0;
+  for (int w = blockIdx.x; ok && w < p.n_pairs; w += gridDim.x, ++it) {
+    const Pair pr = decode_pair(w, p);
+    const int buf = it & 1;
+    for (int s = 0; s < kSlots && ok; ++s) {
+      if (pr.count[s] == 0) continue;
+      ok = mbar_wait(&b.q_empty[s][buf], (q_uses[s][buf] & 1) ^ 1, abort,
+                     p.status, VEDA_STATUS_TIMEOUT);
       if (!ok) break;
-      mbar_expect_tx(&b.k_full[stage], kKBytes);
-      tma_load_2d(km, smem + kSmemK + stage * kKBytes, &b.k_full[stage], 0,
-                  it.head * n_slots + t * kTile);
-      ++gk;
-      ok = mbar_wait(&b.v_empty[stage], ph ^ 1, abort, p.status,
-                     VEDA_STATUS_TIMEOUT);
-      if (!ok) break;
-      mbar_expect_tx(&b.v_full[stage], kVBytes);
-      uint8_t* vdst = smem + kSmemV + stage * kVBytes;
-      tma_load_3d(vm, vdst, &b.v_full[stage], 0, it.head, t * kTile);
-      tma_load_3d(vm, vdst + kVBytes / 2, &b.v_full[stage], 64, it.head,
-                  t * kTile);
-      ++gv;
+      mbar_expect_tx(&b.q_full[s][buf], kQBytes);
+      tma_load_2d(qm, q_tile(smem, s, buf), &b.q_full[s][buf], 0,
+                  pr.head * n_slots + pr.qt[s] * kTile);
+      ++q_uses[s][buf];
+    }
+    const int steps = max(pr.count[0], pr.count[1]);
+    for (int j = 0; j < steps && ok; ++j) {
+      for (int s = 0; s < kSlots && ok; ++s) {
+        if (j >= pr.count[s]) continue;
+        int t = __ldg(pr.idx[s] + j);
+        if (t < 0 || t >= p.n_tiles) report(p.status, VEDA_STATUS_BAD_INDEX);
+        t = clamp_tile(t, p.n_tiles);
+        const int stage = gk % kStages;
+        const uint32_t ph = (gk / kStages) & 1;
+        ok = mbar_wait(&b.k_empty[stage], ph ^ 1, abort, p.status,
+                       VEDA_STATUS_TIMEOUT);
+        if (!ok) break;
+        mbar_expect_tx(&b.k_full[stage], kKBytes);
+        tma_load_2d(km, smem + kSmemK + stage * kKBytes, &b.k_full[stage], 0,
+                    pr.head * n_slots + t * kTile);
+        ++gk;
+        ok = mbar_wait(&b.v_empty[stage], ph ^ 1, abort, p.status,
+                       VEDA_STATUS_TIMEOUT);
+        if (!ok) break;
+        mbar_expect_tx(&b.v_full[stage], kVBytes);
+        uint8_t* vdst = smem + kSmemV + stage * kVBytes;
+        tma_load_3d(vm, vdst, &b.v_full[stage], 0, pr.head, t * kTile);
+        tma_load_3d(vm, vdst + kVBytes / 2, &b.v_full[stage], 64, pr.head,
+                    t * kTile);
+        ++gv;
+      }
     }
   }
   // Let every copy this CTA started land before it can exit.
-  for (int m = n - 2; m < n; ++m)
-    if (m >= 0) drain_wait(&b.q_full[m & 1], (m >> 1) & 1, p.status);
+  for (int s = 0; s < kSlots; ++s)
+    for (int buf = 0; buf < 2; ++buf)
+      if (q_uses[s][buf] > 0)
+        drain_wait(&b.q_full[s][buf], (q_uses[s][buf] - 1) & 1, p.status);
   for (int g = gk - kStages; g < gk; ++g)
     if (g >= 0) drain_wait(&b.k_full[g % kStages], (g / kStages) & 1, p.status);
   for (int g = gv - kStages; g < gv; ++g)
     if (g >= 0) drain_wait(&b.v_full[g % kStages], (g / kStages) & 1, p.status);
 }
 
-// Warp 2, one thread: S[g % 2] = Q K^T for every tile g, as soon as its K
-// is in and both halves' P V that last read S[g % 2] (tile g - 2) are done.
-__device__ __forceinline__ void issue_qk(uint8_t* smem, Barriers& b, uint32_t tmem,
-                         const AttnParams& p) {
+// Warp 1, one thread: every tcgen05.mma of the CTA, in a fixed interleave
+// of the two slots.
+template <typename VT>
+__device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
+                          const AttnParams& p) {
   volatile int* abort = &b.abort;
   constexpr uint32_t idesc_qk = idesc(2, 1, 0, 128, 128);
-  int n = 0, g = 0;
-  bool ok = true;
-  for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
-    const Item it = decode_item(w, p);
-    if (it.count == 0) continue;
-    ok = mbar_wait(&b.q_full[n & 1], (n >> 1) & 1, abort, p.status,
-                   VEDA_STATUS_TIMEOUT);
-    const uint64_t q_desc =
-        smem_desc_sw128(smem_u32(smem + kSmemQ + (n & 1) * kQBytes), 16, 1024);
-    for (int j = 0; j < it.count && ok; ++j, ++g) {
-      for (int h = 0; h < 2 && ok && g >= 2; ++h)
-        ok = mbar_wait(&b.pv_done[h][g & 1], ((g - 2) >> 1) & 1, abort,
-                       p.status, VEDA_STATUS_TIMEOUT);
-      const int stage = g % kStages;
-      if (ok)
-        ok = mbar_wait(&b.k_full[stage], (g / kStages) & 1, abort, p.status,
-                       VEDA_STATUS_TIMEOUT);
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t d = tmem + tmem_s(g & 1);
-      const uint64_t k_desc =
-          smem_desc_sw128(smem_u32(smem + kSmemK + stage * kKBytes), 16, 1024);
-      mma_i8_ss(d, q_desc, k_desc, idesc_qk, 0u);
-#pragma unroll
-      for (int kk = 1; kk < 4; ++kk)  // K = 32 bytes per instruction
-        mma_i8_ss(d, q_desc + 2 * kk, k_desc + 2 * kk, idesc_qk, 1u);
-      tc_commit(&b.k_empty[stage]);
-      tc_commit(&b.s_full[g & 1]);
-    }
-    if (ok) tc_commit(&b.q_empty[n & 1]);  // the item's last Q K^T
-    ++n;
-  }
-  tc_commit(&b.fin[0]);
-  drain_wait(&b.fin[0], 0, p.status);
-}
-
-// Warp 1, one thread: O_h (+)= P_h V_h for both key halves of every tile
-// g once that half's P is written; the first P V of an item waits until
-// the previous item's rows have been read out of O_0 and O_1.
-template <typename VT>
-__device__ __forceinline__ void issue_pv(uint8_t* smem, Barriers& b, uint32_t tmem,
-                         const AttnParams& p) {
-  volatile int* abort = &b.abort;
   constexpr uint32_t idesc_pv = idesc(1, Pack<VT>::kFormat, 1, 128, 128);
-  int n = 0, g = 0;
+  int q_uses[kSlots][2] = {{0, 0}, {0, 0}};
+  int tiles[kSlots] = {0, 0};  // P tiles taken per slot (p_full phases)
+  int items[kSlots] = {0, 0};  // walks finished per slot (o_free phases)
+  int gk = 0, gv = 0;          // K / V ring positions
   bool ok = true;
-  for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
-    const Item it = decode_item(w, p);
-    if (it.count == 0) continue;
-    for (int j = 0; j < it.count && ok; ++j, ++g) {
-      const int stage = g % kStages;
-      for (int h = 0; h < 2 && ok; ++h) {
-        ok = mbar_wait(&b.p_full[h][g & 1], (g >> 1) & 1, abort, p.status,
-                       VEDA_STATUS_TIMEOUT);
-        if (ok && j == 0 && h == 0 && n >= 1)
-          ok = mbar_wait(&b.o_free, (n - 1) & 1, abort, p.status,
-                         VEDA_STATUS_TIMEOUT);
-        if (ok && h == 0)
-          ok = mbar_wait(&b.v_full[stage], (g / kStages) & 1, abort, p.status,
-                         VEDA_STATUS_TIMEOUT);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t o = tmem + tmem_o(h);
-        const uint32_t a = tmem + tmem_s(g & 1) + 64 * h;
-        const uint64_t v_desc = smem_desc_sw128(
-            smem_u32(smem + kSmemV + stage * kVBytes), kVBytes / 2, 1024);
-        mma_f16_ts(o, a, v_desc + static_cast<uint64_t>(h * 512), idesc_pv,
-                   j > 0 ? 1u : 0u);
+
+  // S[s] = Q[s] K^T of the next K in the ring; frees the K stage, signals S.
+  auto qk = [&](int s, int buf) {
+    const int stage = gk % kStages;
+    if (!mbar_wait(&b.k_full[stage], (gk / kStages) & 1, abort, p.status,
+                   VEDA_STATUS_TIMEOUT))
+      return false;
+    tc_fence_after();
+    const uint64_t q_desc =
+        smem_desc_sw128(smem_u32(q_tile(smem, s, buf)), 16, 1024);
+    const uint64_t k_desc =
+        smem_desc_sw128(smem_u32(smem + kSmemK + stage * kKBytes), 16, 1024);
 #pragma unroll
-        for (int kk = 1; kk < 4; ++kk)  // 16 keys (8 TMEM columns of P) each
-          mma_f16_ts(o, a + 8 * kk,
-                     v_desc + static_cast<uint64_t>((4 * h + kk) * 128),
-                     idesc_pv, 1u);
-        if (h == 1) tc_commit(&b.v_empty[stage]);
-        tc_commit(&b.pv_done[h][g & 1]);
+    for (int kk = 0; kk < 4; ++kk)  // K = 32 bytes per instruction
+      mma_i8_ss(tmem + tmem_s(s), q_desc + 2 * kk, k_desc + 2 * kk, idesc_qk,
+                kk > 0 ? 1u : 0u);
+    tc_commit(&b.k_empty[stage]);
+    tc_commit(&b.s_full[s]);
+    ++gk;
+    return true;
+  };
+  // O[s] (+)= P[s] V of the next V in the ring; frees the V stage.
+  auto pv = [&](int s, bool accumulate) {
+    const int stage = gv % kStages;
+    if (!mbar_wait(&b.v_full[stage], (gv / kStages) & 1, abort, p.status,
+                   VEDA_STATUS_TIMEOUT))
+      return false;
+    tc_fence_after();
+    const uint64_t v_desc = smem_desc_sw128(
+        smem_u32(smem + kSmemV + stage * kVBytes), kVBytes / 2, 1024);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)  // 16 keys (8 TMEM columns of P) each
+      mma_f16_ts(tmem + tmem_o(s), tmem + tmem_s(s) + 8 * kk,
+                 v_desc + static_cast<uint64_t>(kk * 128), idesc_pv,
+                 (accumulate || kk > 0) ? 1u : 0u);
+    tc_commit(&b.v_empty[stage]);
+    ++gv;
+    return true;
+  };
+
+  int it = 0;
+  for (int w = blockIdx.x; ok && w < p.n_pairs; w += gridDim.x, ++it) {
+    const Pair pr = decode_pair(w, p);
+    const int buf = it & 1;
+    for (int s = 0; s < kSlots && ok; ++s) {
+      if (pr.count[s] == 0) continue;
+      ok = mbar_wait(&b.q_full[s][buf], q_uses[s][buf] & 1, abort, p.status,
+                     VEDA_STATUS_TIMEOUT);
+      ++q_uses[s][buf];
+      if (ok) ok = qk(s, buf);
+    }
+    const int steps = max(pr.count[0], pr.count[1]);
+    for (int j = 0; j < steps && ok; ++j) {
+      for (int s = 0; s < kSlots && ok; ++s) {
+        if (j >= pr.count[s]) continue;
+        ok = mbar_wait(&b.p_full[s], tiles[s] & 1, abort, p.status,
+                       VEDA_STATUS_TIMEOUT);
+        ++tiles[s];
+        // the first P V of a walk overwrites O: the last walk's rows must
+        // have been read out of it
+        if (ok && j == 0 && items[s] > 0)
+          ok = mbar_wait(&b.o_free[s], (items[s] - 1) & 1, abort, p.status,
+                         VEDA_STATUS_TIMEOUT);
+        if (ok) ok = pv(s, j > 0);
+        if (!ok) break;
+        if (j + 1 < pr.count[s]) {
+          ok = qk(s, buf);
+        } else {
+          tc_commit(&b.o_ready[s]);
+          tc_commit(&b.q_empty[s][buf]);
+          ++items[s];
+        }
       }
     }
-    if (ok) tc_commit(&b.o_ready);
-    ++n;
   }
-  tc_commit(&b.fin[1]);
-  drain_wait(&b.fin[1], 0, p.status);
+  // Every MMA this CTA issued completes before TMEM is released.
+  tc_commit(&b.fin);
+  drain_wait(&b.fin, 0, p.status);
 }
 
 template <typename VT>
@@ -311,6 +335,16 @@ __device__ void store_row(VT* dst, const float* v) {
   }
 }
 
+// Per-tile constants of the softmax: the two K-half scales folded with the
+// Q scale, the magic-number offsets that go with them, the valid rows. The
+// global loads behind them (K scales, valid count, next tile id) are issued
+// a step before the tile that uses them.
+struct TileMeta {
+  float sc0, sc1;    // q_scale * k_scale of key rows 0-63 / 64-127
+  float off0, off1;  // 1.5 * 2^23 * sc0 / sc1
+  int valid;
+};
+
 // int32 S + 0x4B400000, read as fp32, is exactly 1.5 * 2^23 + S for
 // |S| < 2^22 (|S| <= 128 * 127 * 127 here), so S * sc - m comes out of one
 // fused multiply-add on the biased value: (1.5 * 2^23 + S) * sc - (off + m).
@@ -320,219 +354,183 @@ __device__ void store_row(VT* dst, const float* v) {
 constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
 
-// Warps 4-7 (key half 0) and 8-11 (key half 1): the softmax of one half of
-// every tile of every item, one row per thread; at the end of each walk the
-// two halves are merged and each warpgroup stores its 64 output columns.
-//
-// The global loads that feed a tile (its K scales and valid count, and the
-// id of the tile after it) are issued a step ahead and consumed a step
-// later, so their latency never sits between two tiles.
 template <typename VT>
-struct HalfSoftmax {
-  Barriers& b;
-  const AttnParams& p;
-  uint32_t lane_addr, o_self;
-  int h, lane;
-  // per walk
-  const int32_t* idx;
-  const float* ks_head;
-  float qs;
-  int count;
-  float m, l;
-  // metadata pipeline (raw values, used one step after their load)
-  float2 ks_cur, ks_next;
-  int valid_cur, valid_next, raw_t1, raw_t2;
-
-  __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) {
-    bool ok = mbar_wait(bar, parity, &b.abort, p.status, VEDA_STATUS_TIMEOUT);
-    return __all_sync(0xffffffffu, ok);
-  }
-
-  __device__ __forceinline__ void load_s(int g, uint32_t* r) {
-    const uint32_t a = lane_addr + tmem_s(g & 1) + 64 * h;
-    tmem_ld32(a, r);
-    tmem_ld32(a + 32, r + 32);
-  }
-
-  // One tile: r holds its S (loaded), rn receives the next tile's S.
-  __device__ __forceinline__ bool step(int j, int g, uint32_t* r,
-                                       uint32_t* rn) {
-    const int t1 = clamp_tile(raw_t1, p.n_tiles);
-    if (j + 1 < count) {
-      ks_next = __ldg(reinterpret_cast<const float2*>(ks_head + 2 * t1));
-      valid_next = __ldg(p.valid + t1);
-    }
-    if (j + 2 < count) raw_t2 = __ldg(idx + j + 2);
-    const float sc = qs * (h ? ks_cur.y : ks_cur.x);
-    const float off = kMagic * sc;
-
-#pragma unroll
-    for (int c = 0; c < 64; ++c) r[c] += kMagicBits;
-    if (valid_cur < 64 * h + 64) {
-#pragma unroll
-      for (int c = 0; c < 64; ++c)
-        if (64 * h + c >= valid_cur) r[c] = 0xFF800000u;  // -inf, p = 0
-    }
-    float ma = -INFINITY, mb = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < 64; c += 4) {
-      ma = max3(ma, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
-      mb = max3(mb, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
-    }
-    const float mt = fmaf(fmaxf(ma, mb), sc, -off);  // this half's max logit
-    const bool need = mt > m + kRescaleThreshold;
-    float alpha = 1.0f;
-    if (need) {
-      alpha = ex2_approx(m - mt);
-      m = mt;
-      l *= alpha;
-    }
-    const uint64_t s2 = f2(sc, sc);
-    const float cn = -(off + m);
-    const uint64_t n2 = f2(cn, cn);
-    uint64_t acc[4] = {0, 0, 0, 0};
-    uint32_t pk[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const uint64_t z =
-          fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
-               s2, n2);
-      float z0, z1;
-      f2_split(z, z0, z1);
-      const float p0 = ex2_approx(z0), p1 = ex2_approx(z1);
-      acc[i & 3] = add2(acc[i & 3], f2(p0, p1));
-      pk[i] = Pack<VT>::two(p0, p1);
-    }
-    tmem_st32(lane_addr + tmem_s(g & 1) + 64 * h, pk);
-    {
-      float a0, a1, a2, a3, a4, a5, a6, a7;
-      f2_split(acc[0], a0, a1);
-      f2_split(acc[1], a2, a3);
-      f2_split(acc[2], a4, a5);
-      f2_split(acc[3], a6, a7);
-      l += ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
-    }
-    // A grown max rescales O_h, which must first hold this half's P V of
-    // the previous tile (rare after the first tiles of a walk).
-    if (j > 0 && __any_sync(0xffffffffu, need)) {
-      if (!wait(&b.pv_done[h][(g - 1) & 1], ((g - 1) >> 1) & 1)) return false;
-      tc_fence_after();
-      const uint64_t a2v = f2(alpha, alpha);
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t o[32];
-        tmem_ld32(o_self + 32 * cc, o);
-        tmem_ld_wait(o);
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float x0, x1;
-          f2_split(mul2(f2(__uint_as_float(o[c]), __uint_as_float(o[c + 1])),
-                        a2v), x0, x1);
-          o[c] = __float_as_uint(x0);
-          o[c + 1] = __float_as_uint(x1);
-        }
-        tmem_st32(o_self + 32 * cc, o);
-      }
-    }
-    tmem_st_wait();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&b.p_full[h][g & 1]);
-    if (j + 1 < count) {
-      if (!wait(&b.s_full[(g + 1) & 1], ((g + 1) >> 1) & 1)) return false;
-      tc_fence_after();
-      load_s(g + 1, rn);
-      tmem_ld_wait(rn);
-      reg_fence32(rn + 32);
-    }
-    ks_cur = ks_next;
-    valid_cur = valid_next;
-    raw_t1 = raw_t2;
-    return true;
-  }
-};
-
-template <typename VT>
-__device__ __forceinline__ void softmax_loop(int h, uint8_t* smem, Barriers& b, uint32_t tmem,
+__device__ void softmax_loop(int slot, Barriers& b, uint32_t tmem,
                              const AttnParams& p, int warp, int lane) {
+  volatile int* abort = &b.abort;
   const int quarter = warp & 3;  // TMEM lanes this warp may access
   const int row = quarter * 32 + lane;
-  HalfSoftmax<VT> sm{b, p};
-  sm.lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-  sm.o_self = sm.lane_addr + tmem_o(h);
-  sm.h = h;
-  sm.lane = lane;
-  const uint32_t o_other = sm.lane_addr + tmem_o(h ^ 1);
-  float2* xch = reinterpret_cast<float2*>(smem + kSmemXch);
-  int n = 0, g = 0;
+  const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+  const uint32_t s_addr = lane_addr + tmem_s(slot);
+  const uint32_t o_addr = lane_addr + tmem_o(slot);
+  int tiles = 0, items = 0;  // phases of s_full / o_ready of this slot
   bool good = true;
-  for (int w = blockIdx.x; good && w < p.n_items; w += gridDim.x) {
-    const Item it = decode_item(w, p);
+  for (int w = blockIdx.x; good && w < p.n_pairs; w += gridDim.x) {
+    const Pair pr = decode_pair(w, p);
+    const int qt = pr.qt[slot];
+    if (qt >= p.n_tiles) continue;
+    const int count = pr.count[slot];
+    const int head = pr.head;
     VT* out = static_cast<VT*>(p.out) +
-              static_cast<int64_t>(it.qt * kTile + row) * p.out_sn +
-              static_cast<int64_t>(it.head) * p.out_sh + 64 * h;
-    if (it.count == 0) {  // nothing kept: the reference's acc / 1 = 0
+              static_cast<int64_t>(qt * kTile + row) * p.out_sn +
+              static_cast<int64_t>(head) * p.out_sh;
+    if (count == 0) {  // nothing kept: the reference's acc / 1 = 0
 #pragma unroll
-      for (int c = 0; c < 64; c += 8)
+      for (int c = 0; c < kDim; c += 8)
         *reinterpret_cast<uint4*>(out + c) = make_uint4(0, 0, 0, 0);
       continue;
     }
-    sm.idx = it.idx;
-    sm.count = it.count;
-    sm.qs = __ldg(p.q_scale + static_cast<int64_t>(it.head) * p.n_tiles + it.qt);
-    sm.ks_head = p.k_scale + static_cast<int64_t>(it.head) * 2 * p.n_tiles;
-    const int t0 = clamp_tile(__ldg(it.idx), p.n_tiles);
-    sm.ks_cur = __ldg(reinterpret_cast<const float2*>(sm.ks_head + 2 * t0));
-    sm.valid_cur = __ldg(p.valid + t0);
-    sm.raw_t1 = it.count > 1 ? __ldg(it.idx + 1) : 0;
-    sm.ks_next = sm.ks_cur;
-    sm.valid_next = sm.valid_cur;
-    sm.raw_t2 = 0;
-    sm.m = -1e30f;
-    sm.l = 0.0f;
+    const int32_t* idx = pr.idx[slot];
+    const float qs = __ldg(p.q_scale + static_cast<int64_t>(head) * p.n_tiles + qt);
+    const float* ks_head = p.k_scale + static_cast<int64_t>(head) * 2 * p.n_tiles;
+    // Metadata runs ahead of the walk: tile ids two steps, scales one
+    // step, so no global load latency sits between two tiles.
+    // Raw loads are issued a step before the values are used.
+    const int t0 = clamp_tile(__ldg(idx), p.n_tiles);
+    float2 ks_cur = __ldg(reinterpret_cast<const float2*>(ks_head + 2 * t0));
+    int valid_cur = __ldg(p.valid + t0);
+    int raw_t1 = count > 1 ? __ldg(idx + 1) : 0, raw_t2 = 0;
+    float2 ks_next = ks_cur;
+    int valid_next = valid_cur;
 
-    uint32_t r[64];
-    good = sm.wait(&b.s_full[g & 1], (g >> 1) & 1);
-    if (!good) break;
-    tc_fence_after();
-    sm.load_s(g, r);
-    tmem_ld_wait(r);
-    reg_fence32(r + 32);
-    for (int j = 0; j < it.count && good; ++j, ++g) good = sm.step(j, g, r, r);
-    if (!good) break;
-    // Merge the halves: exchange (m, l), then O = sum_h O_h 2^(m_h - M) /
-    // sum_h l_h 2^(m_h - M) for this warpgroup's 64 output columns.
-    float2* slot = xch + (n & 1) * 2 * kTile;
-    slot[h * kTile + row] = make_float2(sm.m, sm.l);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&b.x_full[n & 1]);
-    good = sm.wait(&b.x_full[n & 1], (n >> 1) & 1) &&
-           sm.wait(&b.o_ready, n & 1);
-    if (!good) break;
-    tc_fence_after();
-    const float2 other = slot[(h ^ 1) * kTile + row];
-    const float mx = fmaxf(sm.m, other.x);
-    const float a_self = ex2_approx(sm.m - mx), a_other = ex2_approx(other.x - mx);
-    const float total = sm.l * a_self + other.y * a_other;
-    const float inv = total > 0.0f ? 1.0f / total : 1.0f;
-    const float w_self = a_self * inv, w_other = a_other * inv;
+    float m = -1e30f, l = 0.0f;
+    for (int j = 0; j < count; ++j) {
+      const int t1 = clamp_tile(raw_t1, p.n_tiles);
+      if (j + 1 < count) {
+        ks_next = __ldg(reinterpret_cast<const float2*>(ks_head + 2 * t1));
+        valid_next = __ldg(p.valid + t1);
+      }
+      if (j + 2 < count) raw_t2 = __ldg(idx + j + 2);
+      TileMeta cur;
+      cur.sc0 = qs * ks_cur.x;
+      cur.sc1 = qs * ks_cur.y;
+      cur.off0 = kMagic * cur.sc0;
+      cur.off1 = kMagic * cur.sc1;
+      cur.valid = valid_cur;
+
+      good = mbar_wait(&b.s_full[slot], tiles & 1, abort, p.status,
+                       VEDA_STATUS_TIMEOUT);
+      ++tiles;
+      if (!__all_sync(0xffffffffu, good)) {
+        good = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[128];
+      tmem_ld32(s_addr + 0, r);
+      tmem_ld32(s_addr + 32, r + 32);
+      tmem_ld32(s_addr + 64, r + 64);
+      tmem_ld32(s_addr + 96, r + 96);
+      tmem_ld_wait(r);
+      reg_fence32(r + 32);
+      reg_fence32(r + 64);
+      reg_fence32(r + 96);
 #pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-      uint32_t os[32], oo[32];
-      tmem_ld32(sm.o_self + 64 * h + 32 * cc, os);
-      tmem_ld32(o_other + 64 * h + 32 * cc, oo);
-      tmem_ld_wait(os);
-      reg_fence32(oo);
+      for (int c = 0; c < 128; ++c) r[c] += kMagicBits;
+      // valid is the tile's (the same in every lane): a warp-uniform branch
+      if (__any_sync(0xffffffffu, cur.valid < kTile)) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c >= cur.valid) r[c] = 0xFF800000u;  // -inf: never the max, p = 0
+      }
+      // row max of each 64-column half on the biased values (monotone in S)
+      float ma0 = -INFINITY, mb0 = -INFINITY, ma1 = -INFINITY,
+            mb1 = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; c += 4) {
+        ma0 = max3(ma0, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
+        mb0 = max3(mb0, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
+        ma1 = max3(ma1, __uint_as_float(r[c + 64]), __uint_as_float(r[c + 65]));
+        mb1 = max3(mb1, __uint_as_float(r[c + 66]), __uint_as_float(r[c + 67]));
+      }
+      const float mt = fmaxf(fmaf(fmaxf(ma0, mb0), cur.sc0, -cur.off0),
+                             fmaf(fmaxf(ma1, mb1), cur.sc1, -cur.off1));
+      const bool need = mt > m + kRescaleThreshold;
+      float alpha = 1.0f;
+      if (need) {
+        alpha = ex2_approx(m - mt);
+        m = mt;
+        l *= alpha;
+      }
+      const uint64_t s0 = f2(cur.sc0, cur.sc0), s1 = f2(cur.sc1, cur.sc1);
+      const float c0 = -(cur.off0 + m), c1 = -(cur.off1 + m);
+      const uint64_t n0 = f2(c0, c0), n1 = f2(c1, c1);
+      uint64_t acc[4] = {0, 0, 0, 0};
+      uint32_t pk[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const uint64_t z =
+            fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+                 i < 32 ? s0 : s1, i < 32 ? n0 : n1);
+        float z0, z1;
+        f2_split(z, z0, z1);
+        const float p0 = ex2_approx(z0), p1 = ex2_approx(z1);
+        acc[i & 3] = add2(acc[i & 3], f2(p0, p1));
+        pk[i] = Pack<VT>::two(p0, p1);
+      }
+      tmem_st32(s_addr + 0, pk);
+      tmem_st32(s_addr + 32, pk + 32);
+      {
+        float a0, a1, a2, a3, a4, a5, a6, a7;
+        f2_split(acc[0], a0, a1);
+        f2_split(acc[1], a2, a3);
+        f2_split(acc[2], a4, a5);
+        f2_split(acc[3], a6, a7);
+        l += ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
+      }
+      // O holds the P V of every earlier tile of this walk (the commit
+      // that signalled S covered them) and is rescaled when a row's max
+      // grew.
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        const uint64_t a2v = f2(alpha, alpha);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + 32 * cc, o);
+          tmem_ld_wait(o);
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float x0, x1;
+            f2_split(mul2(f2(__uint_as_float(o[c]), __uint_as_float(o[c + 1])),
+                          a2v), x0, x1);
+            o[c] = __float_as_uint(x0);
+            o[c + 1] = __float_as_uint(x1);
+          }
+          tmem_st32(o_addr + 32 * cc, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b.p_full[slot]);
+      ks_cur = ks_next;
+      valid_cur = valid_next;
+      raw_t1 = raw_t2;
+    }
+    if (!good) break;
+    good = mbar_wait(&b.o_ready[slot], items & 1, abort, p.status,
+                     VEDA_STATUS_TIMEOUT);
+    ++items;
+    if (!__all_sync(0xffffffffu, good)) {
+      good = false;
+      break;
+    }
+    tc_fence_after();
+    const float inv = l > 0.0f ? 1.0f / l : 1.0f;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t o[32];
+      tmem_ld32(o_addr + 32 * cc, o);
+      tmem_ld_wait(o);
       float v[32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        v[c] = __uint_as_float(os[c]) * w_self + __uint_as_float(oo[c]) * w_other;
+      for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(o[c]) * inv;
       store_row<VT>(out + 32 * cc, v);
     }
+    // O of this slot may now be overwritten by the next walk's first P V.
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&b.o_free);
-    ++n;
+    if (lane == 0) mbar_arrive(&b.o_free[slot]);
   }
 }
 
@@ -559,25 +557,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // The 128-byte swizzle pattern assumes 1024-byte aligned tiles.
     b.abort = (smem_u32(smem) & 1023u) != 0 ? 1 : 0;
     if (b.abort) report(p.status, VEDA_STATUS_MISALIGNED);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&b.q_full[i], 1);
-      mbar_init(&b.q_empty[i], 1);
-      mbar_init(&b.s_full[i], 1);
-      mbar_init(&b.x_full[i], 8);
-      mbar_init(&b.fin[i], 1);
-      for (int h = 0; h < 2; ++h) {
-        mbar_init(&b.p_full[h][i], 4);
-        mbar_init(&b.pv_done[h][i], 1);
+    for (int s = 0; s < kSlots; ++s) {
+      for (int buf = 0; buf < 2; ++buf) {
+        mbar_init(&b.q_full[s][buf], 1);
+        mbar_init(&b.q_empty[s][buf], 1);
       }
+      mbar_init(&b.s_full[s], 1);
+      mbar_init(&b.p_full[s], 4);
+      mbar_init(&b.o_ready[s], 1);
+      mbar_init(&b.o_free[s], 4);
     }
-    mbar_init(&b.o_ready, 1);
-    mbar_init(&b.o_free, 8);
     for (int st = 0; st < kStages; ++st) {
       mbar_init(&b.k_full[st], 1);
       mbar_init(&b.k_empty[st], 1);
       mbar_init(&b.v_full[st], 1);
       mbar_init(&b.v_empty[st], 1);
     }
+    mbar_init(&b.fin, 1);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(&b.tmem_base, kTmemCols);
@@ -588,16 +584,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const bool run = b.abort == 0;
 
   if (warp < 4) {
-    regs_dec<kIssueRegs>();
-    if (run && lane == 0) {
-      if (warp == 0) produce(&q_map, &k_map, &v_map, smem, b, p);
-      if (warp == 1) issue_pv<VT>(smem, b, tmem, p);
-      if (warp == 2) issue_qk(smem, b, tmem, p);
+    regs_dec<kLowRegs>();
+    if (run && warp == 0) {
+      if (lane == 0) produce(&q_map, &k_map, &v_map, smem, b, p);
+      __syncwarp();
+    } else if (run && warp == 1) {
+      if (lane == 0) issue_mma<VT>(smem, b, tmem, p);
+      __syncwarp();
     }
-    __syncwarp();
   } else {
-    regs_inc<kSoftmaxRegs>();
-    if (run) softmax_loop<VT>((warp - 4) >> 2, smem, b, tmem, p, warp, lane);
+    regs_inc<kHighRegs>();
+    if (run) softmax_loop<VT>((warp - 4) >> 2, b, tmem, p, warp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -628,7 +625,7 @@ int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     if (device >= 0 && device < 64) g_smem_set[dt][device].store(1);
   }
-  const int grid = p.n_items < sms ? p.n_items : sms;
+  const int grid = p.n_pairs < sms ? p.n_pairs : sms;
   sparse_attention_kernel<VT><<<grid, kAttnThreads, kSmemBytes, stream>>>(
       qm, km, vm, p);
   VEDA_CHECK_CUDA(cudaGetLastError());
@@ -704,7 +701,7 @@ extern "C" int veda_sparse_attention(
   p.n_tiles = n_tiles;
   p.width = width;
   p.heads = heads;
-  p.n_items = heads * n_tiles;
+  p.n_pairs = heads * ((n_tiles + 1) / 2);
   p.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (v_dtype == VEDA_BF16) return launch<__nv_bfloat16>(qm, km, vm, p, s, 0);
