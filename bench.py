@@ -190,7 +190,7 @@ class Call:
     """One Veda attention call on this rank's heads (the timed step)."""
 
     def __init__(self, n_local: int, device, group=None, world=1):
-        from veda_b200 import kernels, selection, tiling
+        from veda_b200 import kernels, selection, sharding, tiling
         self.kernels = kernels
         self.layout = tiling.identity_layout(REAL, device)
         self.blocks = selection.column_blocks(
@@ -202,12 +202,40 @@ class Call:
         self.device = device
         self.group, self.world = group, world
         self.quant = {}
-        self.out = torch.empty(SEQ, n_local, DIM, dtype=torch.bfloat16,
-                               device=device)
-        self.gathered = torch.empty(world, SEQ, n_local, DIM,
-                                    dtype=torch.bfloat16, device=device) \
-            if world > 1 else None
         self.pre = DIM ** -0.5 * kernels.LOG2E
+        self.mc = None
+        self.out_mc = 0
+        self.gathered = None
+        self.mc_error = None
+        if world > 1 and sharding.MulticastOutput.supported(device):
+            # the output exchange is folded into the attention kernel
+            rank = torch.distributed.get_rank(group)
+            lo, hi = sharding.head_range(HEADS, rank, world)
+            try:
+                self.mc = sharding.MulticastOutput(
+                    (SEQ, HEADS, DIM), torch.bfloat16, device, group)
+            except Exception as error:  # no multicast object: use NCCL
+                self.mc_error = str(error).splitlines()[0][:200]
+        if self.mc is not None:
+            self.out = self.mc.local_view(lo, hi)
+            self.out_mc = self.mc.multicast_address(self.out)
+        else:
+            self.out = torch.empty(SEQ, n_local, DIM, dtype=torch.bfloat16,
+                                   device=device)
+            if world > 1:
+                self.gathered = torch.empty(world, SEQ, n_local, DIM,
+                                            dtype=torch.bfloat16,
+                                            device=device)
+
+    @property
+    def exchange(self) -> str:
+        if self.world == 1:
+            return 'none'
+        if self.mc is not None:
+            return 'multimem'
+        return 'nccl all-gather' + (f' (multicast unavailable: '
+                                    f'{self.mc_error})' if self.mc_error
+                                    else '')
 
     def __call__(self, s: dict, events=None):
         from veda_b200 import ops
@@ -222,13 +250,33 @@ class Call:
         rec(2)
         ops.sparse_attention(quant['q_i8'], quant['q_scale'], quant['k_i8'],
                              quant['k_scale'], s['v'], index, count,
-                             self.layout.valid_count, out=self.out)
+                             self.layout.valid_count, out=self.out,
+                             out_multicast=self.out_mc)
         rec(3)
-        if self.gathered is not None:
+        if self.mc is not None:
+            self.mc.complete()
+        elif self.gathered is not None:
             torch.distributed.all_gather_into_tensor(self.gathered, self.out,
                                                      group=self.group)
         rec(4)
         return count
+
+    def check_exchange(self, s: dict) -> bool:
+        """The multicast output equals an NCCL all-gather of the plain
+        kernel's per-rank outputs, bit for bit (untimed self-check)."""
+        from veda_b200 import ops, sharding
+        self(s)
+        full = self.mc.complete().clone()
+        index, count = ops.select_index(s['scores'], self.layout.kv_ok,
+                                        N_TILES, self.spec, self.extra,
+                                        self.width)
+        quant = ops.quant_pool(s['q'], s['k'], self.layout.valid_count, 0,
+                               self.pre, pool=False)
+        local = ops.sparse_attention(quant['q_i8'], quant['q_scale'],
+                                     quant['k_i8'], quant['k_scale'], s['v'],
+                                     index, count, self.layout.valid_count)
+        want = sharding.assemble(sharding.gather_heads(local, self.group))
+        return bool(torch.equal(full, want))
 
 
 def cpu_reference(seconds_hint: float = 15.0) -> dict:
@@ -313,6 +361,10 @@ def main():
     group = None
     if world > 1:
         import datetime
+        # NCCL's version banner goes to stdout, where only the JSON line
+        # belongs
+        if os.environ.get('NCCL_DEBUG', 'VERSION').upper() == 'VERSION':
+            os.environ['NCCL_DEBUG'] = 'WARN'
         torch.distributed.init_process_group(
             'nccl', device_id=device, timeout=datetime.timedelta(seconds=120))
         group = torch.distributed.group.WORLD
@@ -325,6 +377,15 @@ def main():
     n_sets = max(2, math.ceil(3 * L2_BYTES / per_set) + 1)
     sets = [make_set(i, heads, device) for i in range(n_sets)]
     call = Call(n_local, device, group, world)
+    exchange_ok = None
+    if call.mc is not None:
+        ok = torch.tensor([1 if call.check_exchange(sets[0]) else 0],
+                          device=device)
+        torch.distributed.all_reduce(ok, torch.distributed.ReduceOp.MIN)
+        exchange_ok = bool(ok.item())
+        if not exchange_ok:
+            raise SystemExit('multicast output differs from the NCCL '
+                             'all-gather')
 
     # exact algorithmic work: kept (query tile, key tile) pairs per set
     pairs = []
@@ -419,11 +480,14 @@ def main():
                        'kept_tiles_per_row': KEEP,
                        'kept_pairs_per_call': total_pairs / args.steps,
                        'parallelism': f'heads/{world}',
+                       'exchange': call.exchange + (
+                           ' (bit-equal to an NCCL all-gather of the same '
+                           'call, checked this run)' if exchange_ok else ''),
                        'l2': f'{n_sets} rotating input sets of '
                              f'{per_set / 2**20:.0f} MB per rank '
                              f'(> L2 between reuses)'},
             'breakdown_ms': {'select': select_ms, 'quant': quant_ms,
-                             'attention': attn_ms, 'all_gather': gather_ms},
+                             'attention': attn_ms, 'exchange': gather_ms},
             'roofline': {
                 'bound': 'tensor', 'kernel': 'sparse_attention_kernel',
                 'achieved': achieved, 'peak': mixed_peak,

@@ -190,6 +190,24 @@ int veda_sparse_attention(const int8_t* q_i8, const float* q_scale,
                           int32_t* status, void* stream);
 
 /*
+ * veda_sparse_attention for head-sharded runs: every output row is stored
+ * once through `out_multicast`, the NVSwitch multicast address of `out`
+ * (the same byte offsets), so each GPU bound to the multicast object ends
+ * up holding every rank's heads. This replaces the all-gather of the
+ * output that head sharding needs (no counterpart in the reference, which
+ * runs on one GPU). The caller orders the stores before reading other
+ * ranks' heads with a collective on the same stream (the kernel ends with
+ * a system-scope fence). `out` is still this rank's buffer.
+ */
+int veda_sparse_attention_multicast(
+    const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
+    const float* k_scale, const void* v, int v_dtype, int64_t v_stride_n,
+    int64_t v_stride_h, const int32_t* index, int width, const int32_t* count,
+    const int32_t* valid_count, int heads, int n_tiles, void* out,
+    void* out_multicast, int64_t out_stride_n, int64_t out_stride_h,
+    int32_t* status, void* stream);
+
+/*
  * Tile-order permutation of packed rows (core/tiling.py:227-242,
  * gather_tiles): out[slot, j, :] = x[perm[slot], heads[j], :], and zero
  * where perm[slot] < 0. x is [seq_len, total_heads, 128] 16-bit with

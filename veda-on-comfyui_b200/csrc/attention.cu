@@ -6,7 +6,7 @@
 // folded in, so these are base-2 logits); key columns at or past the tile's
 // valid count are masked; online softmax with exp2; O += P V; out = O / l.
 //
-// B200 mapping: a persistent CTA per SM (384 threads, 208 KB of shared
+// B200 mapping: a persistent CTA per SM (384 threads, 225 KB of shared
 // memory, all 512 TMEM columns) walks pairs of query tiles of one head, the
 // two tiles ("slots" A and B) each with its own key-tile list:
 //   warp 0       TMA producer: per pair the two Q tiles (int8, double
@@ -46,8 +46,14 @@ constexpr uint32_t kVBytes = kTile * kDim * 2;  // 16-bit V tile
 constexpr uint32_t kSmemQ = 0;                  // [slot][buffer] Q tiles
 constexpr uint32_t kSmemK = kSmemQ + 4 * kQBytes;
 constexpr uint32_t kSmemV = kSmemK + kStages * kKBytes;
-constexpr uint32_t kSmemBar = kSmemV + kStages * kVBytes;
+// Per softmax warp, 32 rows x 64 bytes: output rows pass through here on
+// their way to a multicast address, so each store moves whole 64-byte row
+// pieces instead of one 16-byte piece per row.
+constexpr uint32_t kStageBytes = 32 * 64;
+constexpr uint32_t kSmemStage = kSmemV + kStages * kVBytes;
+constexpr uint32_t kSmemBar = kSmemStage + 8 * kStageBytes;
 constexpr uint32_t kSmemBytes = kSmemBar + 512;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory over the limit");
 constexpr uint32_t kTmemCols = 512;
 // O is rescaled only when a row's max grows by more than this (log2 units),
 // so P stays below 2^8 and the final O / l is unchanged.
@@ -82,6 +88,7 @@ struct AttnParams {
   const int32_t* count;  // [H][n_tiles]
   const int32_t* valid;  // [n_tiles]
   void* out;
+  void* out_mc;          // multicast address of out (element 0), or null
   int64_t out_sn, out_sh;
   int n_tiles, width, heads;
   int n_pairs;           // heads * ceil(n_tiles / 2)
@@ -322,6 +329,43 @@ __device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
   drain_wait(&b.fin, 0, p.status);
 }
 
+// 16 bytes to every GPU bound to the multicast object behind `mc` (one
+// store through NVSwitch; the bytes are moved, not interpreted).
+__device__ __forceinline__ void store_multicast(void* mc, uint4 u) {
+  asm volatile(
+      "multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
+      "f"(__uint_as_float(u.x)), "f"(__uint_as_float(u.y)),
+      "f"(__uint_as_float(u.z)), "f"(__uint_as_float(u.w))
+      : "memory");
+}
+
+// Columns [32 cc, 32 cc + 32) of the warp's 32 rows (v: this lane's row)
+// through the multicast address: staged in shared memory, then written as
+// eight 64-byte row pieces per instruction. mc0 is the warp's first row.
+template <typename VT>
+__device__ void store_rows_multicast(uint8_t* stage, VT* mc0, int64_t row_sn,
+                                     int cc, int lane, const float* v) {
+  uint4* mine = reinterpret_cast<uint4*>(stage + lane * 64);
+#pragma unroll
+  for (int c = 0; c < 32; c += 8) {
+    uint4 u;
+    u.x = Pack<VT>::two(v[c], v[c + 1]);
+    u.y = Pack<VT>::two(v[c + 2], v[c + 3]);
+    u.z = Pack<VT>::two(v[c + 4], v[c + 5]);
+    u.w = Pack<VT>::two(v[c + 6], v[c + 7]);
+    mine[c / 8] = u;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 8 * i + (lane >> 2), piece = lane & 3;
+    const uint4 u = *reinterpret_cast<const uint4*>(stage + r * 64 + piece * 16);
+    store_multicast(mc0 + r * row_sn + 32 * cc + 8 * piece, u);
+  }
+  __syncwarp();
+}
+
+// 32 outputs of a row, to local memory.
 template <typename VT>
 __device__ void store_row(VT* dst, const float* v) {
 #pragma unroll
@@ -355,9 +399,11 @@ constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
 
 template <typename VT>
-__device__ void softmax_loop(int slot, Barriers& b, uint32_t tmem,
-                             const AttnParams& p, int warp, int lane) {
+__device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
+                             uint32_t tmem, const AttnParams& p, int warp,
+                             int lane) {
   volatile int* abort = &b.abort;
+  uint8_t* stage = smem + kSmemStage + (warp - 4) * kStageBytes;
   const int quarter = warp & 3;  // TMEM lanes this warp may access
   const int row = quarter * 32 + lane;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -371,13 +417,26 @@ __device__ void softmax_loop(int slot, Barriers& b, uint32_t tmem,
     if (qt >= p.n_tiles) continue;
     const int count = pr.count[slot];
     const int head = pr.head;
-    VT* out = static_cast<VT*>(p.out) +
-              static_cast<int64_t>(qt * kTile + row) * p.out_sn +
-              static_cast<int64_t>(head) * p.out_sh;
+    const int64_t out_off = static_cast<int64_t>(qt * kTile + row) * p.out_sn +
+                            static_cast<int64_t>(head) * p.out_sh;
+    VT* out = static_cast<VT*>(p.out) + out_off;
+    VT* out_mc = p.out_mc != nullptr ? static_cast<VT*>(p.out_mc) + out_off
+                                     : nullptr;
+    // the warp's first row through the multicast address
+    VT* mc0 = out_mc != nullptr ? out_mc - lane * p.out_sn : nullptr;
     if (count == 0) {  // nothing kept: the reference's acc / 1 = 0
+      if (mc0 != nullptr) {
+        float zero[32];
 #pragma unroll
-      for (int c = 0; c < kDim; c += 8)
-        *reinterpret_cast<uint4*>(out + c) = make_uint4(0, 0, 0, 0);
+        for (int c = 0; c < 32; ++c) zero[c] = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          store_rows_multicast<VT>(stage, mc0, p.out_sn, cc, lane, zero);
+      } else {
+#pragma unroll
+        for (int c = 0; c < kDim; c += 8)
+          *reinterpret_cast<uint4*>(out + c) = make_uint4(0, 0, 0, 0);
+      }
       continue;
     }
     const int32_t* idx = pr.idx[slot];
@@ -525,13 +584,19 @@ __device__ void softmax_loop(int slot, Barriers& b, uint32_t tmem,
       float v[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(o[c]) * inv;
-      store_row<VT>(out + 32 * cc, v);
+      if (mc0 != nullptr)
+        store_rows_multicast<VT>(stage, mc0, p.out_sn, cc, lane, v);
+      else
+        store_row<VT>(out + 32 * cc, v);
     }
     // O of this slot may now be overwritten by the next walk's first P V.
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&b.o_free[slot]);
   }
+  // Multicast rows are ordered before whatever the host does next to
+  // signal the other GPUs (a collective on the same stream).
+  if (p.out_mc != nullptr) __threadfence_system();
 }
 
 template <uint32_t N>
@@ -594,7 +659,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     regs_inc<kHighRegs>();
-    if (run) softmax_loop<VT>((warp - 4) >> 2, b, tmem, p, warp, lane);
+    if (run) softmax_loop<VT>((warp - 4) >> 2, smem, b, tmem, p, warp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -637,13 +702,15 @@ int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
 
 using namespace veda;
 
-extern "C" int veda_sparse_attention(
-    const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
-    const float* k_scale, const void* v, int v_dtype, int64_t v_stride_n,
-    int64_t v_stride_h, const int32_t* index, int width, const int32_t* count,
-    const int32_t* valid_count, int heads, int n_tiles, void* out,
-    int64_t out_stride_n, int64_t out_stride_h, int32_t* status,
-    void* stream) {
+namespace {
+
+int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
+           const float* k_scale, const void* v, int v_dtype,
+           int64_t v_stride_n, int64_t v_stride_h, const int32_t* index,
+           int width, const int32_t* count, const int32_t* valid_count,
+           int heads, int n_tiles, void* out, void* out_mc,
+           int64_t out_stride_n, int64_t out_stride_h, int32_t* status,
+           void* stream) {
   if (int rc = check_device()) return rc;
   if (heads <= 0 || heads > 65535 || n_tiles <= 0 || width <= 0)
     return fail(VEDA_ERR_INVALID, "bad sizes: heads %d, n_tiles %d, width %d",
@@ -696,6 +763,7 @@ extern "C" int veda_sparse_attention(
   p.count = count;
   p.valid = valid_count;
   p.out = out;
+  p.out_mc = out_mc;
   p.out_sn = out_stride_n;
   p.out_sh = out_stride_h;
   p.n_tiles = n_tiles;
@@ -706,4 +774,34 @@ extern "C" int veda_sparse_attention(
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (v_dtype == VEDA_BF16) return launch<__nv_bfloat16>(qm, km, vm, p, s, 0);
   return launch<__half>(qm, km, vm, p, s, 1);
+}
+
+}  // namespace
+
+extern "C" int veda_sparse_attention(
+    const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
+    const float* k_scale, const void* v, int v_dtype, int64_t v_stride_n,
+    int64_t v_stride_h, const int32_t* index, int width, const int32_t* count,
+    const int32_t* valid_count, int heads, int n_tiles, void* out,
+    int64_t out_stride_n, int64_t out_stride_h, int32_t* status,
+    void* stream) {
+  return attend(q_i8, q_scale, k_i8, k_scale, v, v_dtype, v_stride_n,
+                v_stride_h, index, width, count, valid_count, heads, n_tiles,
+                out, nullptr, out_stride_n, out_stride_h, status, stream);
+}
+
+extern "C" int veda_sparse_attention_multicast(
+    const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
+    const float* k_scale, const void* v, int v_dtype, int64_t v_stride_n,
+    int64_t v_stride_h, const int32_t* index, int width, const int32_t* count,
+    const int32_t* valid_count, int heads, int n_tiles, void* out,
+    void* out_multicast, int64_t out_stride_n, int64_t out_stride_h,
+    int32_t* status, void* stream) {
+  if (out_multicast == nullptr || !aligned16(out_multicast))
+    return fail(VEDA_ERR_INVALID, "out_multicast must be a 16-byte aligned "
+                                  "multicast address");
+  return attend(q_i8, q_scale, k_i8, k_scale, v, v_dtype, v_stride_n,
+                v_stride_h, index, width, count, valid_count, heads, n_tiles,
+                out, out_multicast, out_stride_n, out_stride_h, status,
+                stream);
 }

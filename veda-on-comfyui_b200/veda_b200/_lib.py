@@ -72,6 +72,9 @@ SIGNATURES = {
     'veda_mask_to_index': [_P, _P, _I, _I, _I, _P, _P, _P, _P],
     'veda_sparse_attention': [_P, _P, _P, _P, _P, _I, _L, _L, _P, _I, _P, _P,
                               _I, _I, _P, _L, _L, _P, _P],
+    'veda_sparse_attention_multicast': [_P, _P, _P, _P, _P, _I, _L, _L, _P,
+                                        _I, _P, _P, _I, _I, _P, _P, _L, _L,
+                                        _P, _P],
     'veda_gather_tiles': [_P, _I, _L, _L, _I, _I, _P, _I, _P, _I, _P, _P],
     'veda_scatter_tiles': [_P, _I, _P, _I, _P, _I, _I, _P, _L, _L, _I, _P],
 }

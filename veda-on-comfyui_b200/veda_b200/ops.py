@@ -220,9 +220,15 @@ def mask_to_index(mask: torch.Tensor, kv_ok: torch.Tensor, width: int):
 
 
 def sparse_attention(q_i8, q_scale, k_i8, k_scale, v, index, count,
-                     valid_count, out: torch.Tensor | None = None):
+                     valid_count, out: torch.Tensor | None = None,
+                     out_multicast: int = 0):
     """INT8 block-sparse attention. v [N, H, 128] 16-bit; returns out
-    [N, H, 128] of v's dtype (or writes `out`, any row / head strides)."""
+    [N, H, 128] of v's dtype (or writes `out`, any row / head strides).
+
+    out_multicast: the NVSwitch multicast address of `out`'s first element
+    (head sharding): rows are stored through it to every GPU bound to the
+    multicast object, instead of to `out` alone.
+    """
     _check_rows(v, 'v')
     device = require_device(q_i8, k_i8, v, index, count, valid_count)
     n, heads, _ = v.shape
@@ -235,11 +241,17 @@ def sparse_attention(q_i8, q_scale, k_i8, k_scale, v, index, count,
     index = index.to(torch.int32).contiguous()
     count = count.to(torch.int32).contiguous()
     valid = valid_count.to(torch.int32).contiguous()
-    _call(device, 'veda_sparse_attention', _ptr(q_i8), _ptr(q_scale), _ptr(k_i8),
-              _ptr(k_scale), _ptr(v), _DTYPES[v.dtype], v.stride(0),
-              v.stride(1), _ptr(index), index.shape[-1], _ptr(count),
-              _ptr(valid), heads, n_tiles, _ptr(out), out.stride(0),
-              out.stride(1), _ptr(status_word(device)), _stream(device))
+    head = (_ptr(q_i8), _ptr(q_scale), _ptr(k_i8), _ptr(k_scale), _ptr(v),
+            _DTYPES[v.dtype], v.stride(0), v.stride(1), _ptr(index),
+            index.shape[-1], _ptr(count), _ptr(valid), heads, n_tiles,
+            _ptr(out))
+    tail = (out.stride(0), out.stride(1), _ptr(status_word(device)),
+            _stream(device))
+    if out_multicast:
+        _call(device, 'veda_sparse_attention_multicast', *head,
+              ctypes.c_void_p(out_multicast), *tail)
+    else:
+        _call(device, 'veda_sparse_attention', *head, *tail)
     return out
 
 

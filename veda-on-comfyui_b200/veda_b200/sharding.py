@@ -10,6 +10,13 @@ rank, as they are in a tensor-parallel DiT block.
 The gathered buffer is [world, N, H_local, D]: rank r's heads at index r.
 `assemble` turns it into [N, H, D] (one copy); consumers that take strided
 input (the scatter back to sequence order) can read the buffer as is.
+
+On GPUs joined by NVSwitch the exchange can be folded into the attention
+kernel instead: `MulticastOutput` holds the full [N, H, D] output in
+symmetric memory bound to a multicast object, each rank's kernel stores its
+heads' rows once through the multicast address (veda_sparse_attention_
+multicast), and one small collective orders the stores before any rank
+reads the others' heads. No separate all-gather runs.
 """
 
 from __future__ import annotations
@@ -76,3 +83,58 @@ class HeadSharded:
                                **sliced, **kwargs)
         gathered = gather_heads(local, self.group)
         return assemble(gathered) if contiguous else gathered
+
+
+class MulticastOutput:
+    """The full [N, H, D] output of a head-sharded call on every rank, written
+    by the ranks' attention kernels through an NVSwitch multicast address.
+
+    Args:
+        shape: (N, H, D) of the full output.
+        dtype, device: Of the output.
+        group: Process group of the ranks (default: the world).
+
+    Raises:
+        RuntimeError: If the device or the group has no multicast support
+            (use `gather_heads` there).
+    """
+
+    def __init__(self, shape, dtype: torch.dtype, device: torch.device,
+                 group=None):
+        import torch.distributed._symmetric_memory as symm
+        self.group = group if group is not None else dist.group.WORLD
+        if not self.supported(device):
+            raise RuntimeError(f'{device} has no multicast support')
+        self.full = symm.empty(*shape, dtype=dtype, device=device)
+        self.handle = symm.rendezvous(self.full, self.group)
+        self.mc_base = int(self.handle.multicast_ptr or 0)
+        if not self.mc_base:
+            raise RuntimeError('the group has no multicast object')
+        self._flag = torch.zeros(1, dtype=torch.int32, device=device)
+
+    @staticmethod
+    def supported(device: torch.device) -> bool:
+        """Whether `device` can bind multicast memory."""
+        try:
+            from torch._C._distributed_c10d import _SymmetricMemory
+            from torch.distributed._symmetric_memory import DeviceType
+            return bool(_SymmetricMemory.has_multicast_support(
+                DeviceType.CUDA, torch.device(device).index or 0))
+        except (ImportError, AttributeError, RuntimeError):
+            return False
+
+    def local_view(self, lo: int, hi: int) -> torch.Tensor:
+        """This rank's heads [lo, hi) of the full buffer ([N, hi - lo, D],
+        strided): the `out` of the multicast attention call."""
+        return self.full[:, lo:hi]
+
+    def multicast_address(self, view: torch.Tensor) -> int:
+        """The multicast address of `view`'s first element."""
+        return self.mc_base + (view.data_ptr() - self.full.data_ptr())
+
+    def complete(self) -> torch.Tensor:
+        """Orders every rank's multicast stores before later work on the
+        current stream (a one-element all-reduce on the same stream), and
+        returns the full output."""
+        dist.all_reduce(self._flag, group=self.group)
+        return self.full
