@@ -63,6 +63,10 @@ constexpr float kRescaleThreshold = 8.0f;
 // each (64512); 128 x 64 + 256 x 216 = 63488 stays within that.
 constexpr uint32_t kLowRegs = 64;
 constexpr uint32_t kHighRegs = 216;
+// setmaxnreg.inc waits until the registers it asks for are free: a split
+// above the launch total (384 threads x 168) would wait forever.
+static_assert(128 * kLowRegs + 256 * kHighRegs <= kAttnThreads * 168,
+              "register split exceeds the CTA's launch allocation");
 
 __host__ __device__ constexpr uint32_t tmem_s(int slot) { return 128u * slot; }
 __host__ __device__ constexpr uint32_t tmem_o(int slot) {
