@@ -322,7 +322,7 @@ def cpu_reference(seconds_hint: float = 15.0) -> dict:
 
 # ---------------------------------------------------------------- main
 
-def run_reference(args, rank: int):
+def run_reference(args, rank: int, json_out):
     if rank != 0:
         return
     samples = []
@@ -343,16 +343,27 @@ def run_reference(args, rank: int):
                              'sample': samples[0]['sample']},
             'e2e': {'value': value, 'unit': 'TFLOPS',
                     'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=json_out, flush=True)
+
+
+def _claim_stdout():
+    """The file the JSON line goes to. Everything else written to file
+    descriptor 1 (NCCL's version banner, library prints) goes to stderr, so
+    stdout carries exactly one line."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), 'w')
+    os.dup2(2, 1)
+    return out
 
 
 def main():
     args = parse_args()
+    json_out = _claim_stdout()
     rank = int(os.environ.get('RANK', 0))
     world = int(os.environ.get('WORLD_SIZE', 1))
     local = int(os.environ.get('LOCAL_RANK', 0))
     if args.impl == 'reference':
-        run_reference(args, rank)
+        run_reference(args, rank, json_out)
         return
     if args.warmup < 3:
         raise SystemExit('--warmup must be at least 3')
@@ -361,10 +372,6 @@ def main():
     group = None
     if world > 1:
         import datetime
-        # NCCL's version banner goes to stdout, where only the JSON line
-        # belongs
-        if os.environ.get('NCCL_DEBUG', 'VERSION').upper() == 'VERSION':
-            os.environ['NCCL_DEBUG'] = 'WARN'
         torch.distributed.init_process_group(
             'nccl', device_id=device, timeout=datetime.timedelta(seconds=120))
         group = torch.distributed.group.WORLD
@@ -507,7 +514,7 @@ def main():
         }
         if world == 1 and not args.no_cpu_baseline:
             line['cpu_baseline'] = cpu_reference()
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=json_out, flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
