@@ -254,12 +254,20 @@ __device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
   int gk = 0, gv = 0;          // K / V ring positions
   bool ok = true;
 
-  // S[s] = Q[s] K^T of the next K in the ring; frees the K stage, signals S.
+  // The next K / V in the ring has landed (this thread consumes both rings
+  // in order, so their parities are unambiguous).
+  auto k_ready = [&]() {
+    return mbar_wait(&b.k_full[gk % kStages], (gk / kStages) & 1, abort,
+                     p.status, VEDA_STATUS_TIMEOUT);
+  };
+  auto v_ready = [&]() {
+    return mbar_wait(&b.v_full[gv % kStages], (gv / kStages) & 1, abort,
+                     p.status, VEDA_STATUS_TIMEOUT);
+  };
+  // S[s] = Q[s] K^T of the next K in the ring (landed); frees the K stage,
+  // signals S.
   auto qk = [&](int s, int buf) {
     const int stage = gk % kStages;
-    if (!mbar_wait(&b.k_full[stage], (gk / kStages) & 1, abort, p.status,
-                   VEDA_STATUS_TIMEOUT))
-      return false;
     tc_fence_after();
     const uint64_t q_desc =
         smem_desc_sw128(smem_u32(q_tile(smem, s, buf)), 16, 1024);
@@ -272,14 +280,10 @@ __device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
     tc_commit(&b.k_empty[stage]);
     tc_commit(&b.s_full[s]);
     ++gk;
-    return true;
   };
-  // O[s] (+)= P[s] V of the next V in the ring; frees the V stage.
+  // O[s] (+)= P[s] V of the next V in the ring (landed); frees the V stage.
   auto pv = [&](int s, bool accumulate) {
     const int stage = gv % kStages;
-    if (!mbar_wait(&b.v_full[stage], (gv / kStages) & 1, abort, p.status,
-                   VEDA_STATUS_TIMEOUT))
-      return false;
     tc_fence_after();
     const uint64_t v_desc = smem_desc_sw128(
         smem_u32(smem + kSmemV + stage * kVBytes), kVBytes / 2, 1024);
@@ -290,7 +294,6 @@ __device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
                  (accumulate || kk > 0) ? 1u : 0u);
     tc_commit(&b.v_empty[stage]);
     ++gv;
-    return true;
   };
 
   int it = 0;
@@ -302,24 +305,31 @@ __device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
       ok = mbar_wait(&b.q_full[s][buf], q_uses[s][buf] & 1, abort, p.status,
                      VEDA_STATUS_TIMEOUT);
       ++q_uses[s][buf];
-      if (ok) ok = qk(s, buf);
+      if (ok) ok = k_ready();
+      if (ok) qk(s, buf);
     }
     const int steps = max(pr.count[0], pr.count[1]);
     for (int j = 0; j < steps && ok; ++j) {
       for (int s = 0; s < kSlots && ok; ++s) {
         if (j >= pr.count[s]) continue;
-        ok = mbar_wait(&b.p_full[s], tiles[s] & 1, abort, p.status,
-                       VEDA_STATUS_TIMEOUT);
+        const bool more = j + 1 < pr.count[s];
+        // V of this tile and K of the next are waited for while the
+        // softmax still works, so P V and Q K^T follow P without delay.
+        ok = v_ready();
+        if (ok && more) ok = k_ready();
+        if (ok)
+          ok = mbar_wait(&b.p_full[s], tiles[s] & 1, abort, p.status,
+                         VEDA_STATUS_TIMEOUT);
         ++tiles[s];
         // the first P V of a walk overwrites O: the last walk's rows must
         // have been read out of it
         if (ok && j == 0 && items[s] > 0)
           ok = mbar_wait(&b.o_free[s], (items[s] - 1) & 1, abort, p.status,
                          VEDA_STATUS_TIMEOUT);
-        if (ok) ok = pv(s, j > 0);
         if (!ok) break;
-        if (j + 1 < pr.count[s]) {
-          ok = qk(s, buf);
+        pv(s, j > 0);
+        if (more) {
+          qk(s, buf);
         } else {
           tc_commit(&b.o_ready[s]);
           tc_commit(&b.q_empty[s][buf]);
