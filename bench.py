@@ -62,6 +62,15 @@ def parse_args():
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--impl', choices=['ours', 'reference'], default='ours')
     p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--config', choices=['cfg1', 'cfg2', 'cfg3', 'cfg4'],
+                   default='cfg1',
+                   help='cfg1 (default): the headline line. cfg2: the '
+                        '48-layer denoising step; cfg3: one layer at '
+                        '--seq-len; cfg4: generated + global reference '
+                        'tiles. cfg2-4 run on one GPU.')
+    p.add_argument('--seq-len', type=int, default=131072,
+                   choices=[16384, 32768, 65536, 131072],
+                   help='cfg3 sequence length')
     return p.parse_args()
 
 
@@ -346,6 +355,113 @@ def run_reference(args, rank: int, json_out):
     print(json.dumps(line), file=json_out, flush=True)
 
 
+def run_config(args, json_out) -> None:
+    """BASELINE configs 2-4 on one GPU (the headline line is cfg1's).
+
+    cfg2  48 sequential layers of cfg1's shape; layers 0, 1 and 47 are
+          full-attention layers (every non-empty key tile), the rest keep
+          26 of 256 tiles. Four independent seeded input sets are cycled
+          over the layers (each 576 MB, so no layer reads the previous
+          one's data from L2). A step is one denoising step (48 calls).
+    cfg3  one layer of H=24 at --seq-len, 90% sparse (ratio budget 0.1).
+    cfg4  24,576 generated tokens (top 32 of 192 tiles) + 8,192 reference
+          tokens tiled as global tiles (every query tile keeps them, and
+          their query tiles keep every tile): variable list lengths.
+    """
+    from veda_b200 import kernels, ops, selection, tiling
+    device = torch.device('cuda', 0)
+    torch.cuda.set_device(device)
+    heads = HEADS
+    if args.config == 'cfg2':
+        seq, real = SEQ, REAL
+        layout = tiling.identity_layout(real, device)
+        budget = selection.Budget(tiles=KEEP)
+        n_layers, full_layers = 48, {0, 1, 47}
+    elif args.config == 'cfg3':
+        seq = real = args.seq_len
+        layout = tiling.identity_layout(real, device)
+        budget = selection.Budget.sparsity(90)
+        n_layers, full_layers = 1, set()
+    else:
+        seq = real = 32768
+        spans = [tiling.TiledSpan(8192, (1, 1, 24576),
+                                  tiling.TileShape(1, 1, 128))]
+        layout = tiling.build_tile_layout(spans, seq, device)
+        budget = selection.Budget(tiles=32)
+        n_layers, full_layers = 1, set()
+    n_tiles, n_video = layout.n_tiles, layout.n_video_tiles
+    blocks = selection.column_blocks(layout, budget,
+                                     selection.Budget(ratio=1.0))
+    dense = selection.dense_index(layout, heads)
+    valid = layout.slot_valid.to(torch.bfloat16)[:, None, None]
+    n_sets = 4 if n_layers > 1 else 2
+    sets = []
+    for i in range(n_sets):
+        g = torch.Generator(device=device)
+        g.manual_seed(70_001 * i + 17)
+        q, k, v = (torch.randn(layout.num_slots, heads, DIM, generator=g,
+                               device=device) for _ in range(3))
+        k = k + torch.randn(heads, DIM, generator=g, device=device) * 2.0
+        sets.append({'q': (q.to(torch.bfloat16) * valid).contiguous(),
+                     'k': (k.to(torch.bfloat16) * valid).contiguous(),
+                     'v': (v.to(torch.bfloat16) * valid).contiguous(),
+                     'scores': torch.rand(heads, n_video, n_video,
+                                          generator=g, device=device)})
+    pre = DIM ** -0.5 * kernels.LOG2E
+    quant_buf = {}
+    out = torch.empty(layout.num_slots, heads, DIM, dtype=torch.bfloat16,
+                      device=device)
+
+    def layer(i):
+        s = sets[i % n_sets]
+        if i in full_layers:
+            index, count = dense
+        else:
+            index, count = selection.select_index(s['scores'], layout, blocks)
+        quant = ops.quant_pool(s['q'], s['k'], layout.valid_count, 0, pre,
+                               pool=False, out=quant_buf)
+        ops.sparse_attention(quant['q_i8'], quant['q_scale'], quant['k_i8'],
+                             quant['k_scale'], s['v'], index, count,
+                             layout.valid_count, out=out)
+        return count
+
+    pairs = sum(int(layer(i).sum().item()) for i in range(n_layers))
+    ops.check_status(device)
+    for _ in range(args.warmup):
+        for i in range(n_layers):
+            layer(i)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(True), torch.cuda.Event(True)
+    start.record()
+    for _ in range(args.steps):
+        for i in range(n_layers):
+            layer(i)
+    end.record()
+    torch.cuda.synchronize()
+    ops.check_status(device)
+    ms = start.elapsed_time(end) / args.steps
+    tflops = pairs * OPS_PER_PAIR / (ms * 1e-3) / 1e12
+    names = {'cfg2': 'attention time per 48-layer denoising step (ms)',
+             'cfg3': f'sparse-attn call latency (ms) at L={seq}, 90% sparse',
+             'cfg4': 'sparse-attn call latency (ms), 24,576 generated + '
+                     '8,192 global reference tokens'}
+    line = {'metric': names[args.config], 'value': ms, 'unit': 'ms',
+            'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': ms, 'higher_is_better': False,
+            'scaling': 'none', 'vs_baseline': None, 'dtype': 'int8+bf16',
+            'data': 'synthetic',
+            'config': {'workload': args.config, 'heads': heads,
+                       'seq_len': seq, 'real_tokens': real,
+                       'n_tiles': n_tiles, 'layers': n_layers,
+                       'full_attention_layers': sorted(full_layers),
+                       'kept_pairs_per_step': pairs,
+                       'l2': f'{n_sets} rotating input sets '
+                             f'(> L2 between reuses)'},
+            'effective_tflops': tflops,
+            'gpu_launches': 3 * n_layers * args.steps}
+    print(json.dumps(line), file=json_out, flush=True)
+
+
 def _claim_stdout():
     """The file the JSON line goes to. Everything else written to file
     descriptor 1 (NCCL's version banner, library prints) goes to stderr, so
@@ -367,6 +483,11 @@ def main():
         return
     if args.warmup < 3:
         raise SystemExit('--warmup must be at least 3')
+    if args.config != 'cfg1':
+        if world > 1:
+            raise SystemExit('--config cfg2-4 run on one GPU')
+        run_config(args, json_out)
+        return
     device = torch.device('cuda', local)
     torch.cuda.set_device(device)
     group = None
