@@ -60,7 +60,12 @@ def parse_args():
     p.add_argument('--gpus', type=int, default=1)
     p.add_argument('--steps', type=int, default=100)
     p.add_argument('--warmup', type=int, default=5)
-    p.add_argument('--impl', choices=['ours', 'reference'], default='ours')
+    p.add_argument('--impl', choices=['ours', 'reference', 'reference-triton'],
+                   default='ours',
+                   help='reference: the reference CPU path on the host '
+                        'cores. reference-triton: the reference package in '
+                        'baseline/_ref, unmodified, on one GPU (its '
+                        'selection and Triton INT8 kernel) at --config.')
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--config', choices=['cfg1', 'cfg2', 'cfg3', 'cfg4'],
                    default='cfg1',
@@ -355,78 +360,98 @@ def run_reference(args, rank: int, json_out):
     print(json.dumps(line), file=json_out, flush=True)
 
 
-def run_config(args, json_out) -> None:
-    """BASELINE configs 2-4 on one GPU (the headline line is cfg1's).
+CONFIG_METRICS = {
+    'cfg1': METRIC,
+    'cfg2': 'attention time per 48-layer denoising step (ms)',
+    'cfg3': 'sparse-attn call latency (ms) at L={seq}, 90% sparse',
+    'cfg4': 'sparse-attn call latency (ms), 24,576 generated + 8,192 '
+            'global reference tokens'}
 
+
+def config_workload(args, device) -> dict:
+    """The layout, budget, layer plan and seeded input sets of one BASELINE
+    config on one GPU. Both GPU arms (`run_config`, `run_reference_gpu`)
+    time exactly these.
+
+    cfg1  one layer, the headline workload (the input sets of `make_set`).
     cfg2  48 sequential layers of cfg1's shape; layers 0, 1 and 47 are
-          full-attention layers (every non-empty key tile), the rest keep
-          26 of 256 tiles. Four independent seeded input sets are cycled
-          over the layers (each 576 MB, so no layer reads the previous
-          one's data from L2). A step is one denoising step (48 calls).
+          full-attention layers, the rest keep 26 of 256 tiles. Four
+          independent seeded input sets are cycled over the layers (each
+          576 MB, so no layer reads the previous one's data from L2). A step
+          is one denoising step (48 calls).
     cfg3  one layer of H=24 at --seq-len, 90% sparse (ratio budget 0.1).
     cfg4  24,576 generated tokens (top 32 of 192 tiles) + 8,192 reference
           tokens tiled as global tiles (every query tile keeps them, and
           their query tiles keep every tile): variable list lengths.
+
+    `spans` is None for rows already in tile order (one 1 x 1 x L span),
+    else (start, grid, tile shape) triples; `budget` is ('tiles', n) or
+    ('sparsity', percent).
     """
-    from veda_b200 import kernels, ops, selection, tiling
-    device = torch.device('cuda', 0)
-    torch.cuda.set_device(device)
-    heads = HEADS
-    if args.config == 'cfg2':
-        seq, real = SEQ, REAL
-        layout = tiling.identity_layout(real, device)
-        budget = selection.Budget(tiles=KEEP)
-        n_layers, full_layers = 48, {0, 1, 47}
-    elif args.config == 'cfg3':
+    from veda_b200 import tiling
+    cfg = args.config
+    spans, n_layers, full_layers = None, 1, set()
+    if cfg in ('cfg1', 'cfg2'):
+        seq, real, budget = SEQ, REAL, ('tiles', KEEP)
+        if cfg == 'cfg2':
+            n_layers, full_layers = 48, {0, 1, 47}
+    elif cfg == 'cfg3':
         seq = real = args.seq_len
-        layout = tiling.identity_layout(real, device)
-        budget = selection.Budget.sparsity(90)
-        n_layers, full_layers = 1, set()
+        budget = ('sparsity', 90)
     else:
         seq = real = 32768
-        spans = [tiling.TiledSpan(8192, (1, 1, 24576),
-                                  tiling.TileShape(1, 1, 128))]
-        layout = tiling.build_tile_layout(spans, seq, device)
-        budget = selection.Budget(tiles=32)
-        n_layers, full_layers = 1, set()
-    n_tiles, n_video = layout.n_tiles, layout.n_video_tiles
-    blocks = selection.column_blocks(layout, budget,
-                                     selection.Budget(ratio=1.0))
-    dense = selection.dense_index(layout, heads)
-    valid = layout.slot_valid.to(torch.bfloat16)[:, None, None]
-    n_sets = 4 if n_layers > 1 else 2
-    sets = []
-    for i in range(n_sets):
-        g = torch.Generator(device=device)
-        g.manual_seed(70_001 * i + 17)
-        q, k, v = (torch.randn(layout.num_slots, heads, DIM, generator=g,
-                               device=device) for _ in range(3))
-        k = k + torch.randn(heads, DIM, generator=g, device=device) * 2.0
-        sets.append({'q': (q.to(torch.bfloat16) * valid).contiguous(),
-                     'k': (k.to(torch.bfloat16) * valid).contiguous(),
-                     'v': (v.to(torch.bfloat16) * valid).contiguous(),
-                     'scores': torch.rand(heads, n_video, n_video,
-                                          generator=g, device=device)})
-    pre = DIM ** -0.5 * kernels.LOG2E
-    quant_buf = {}
-    out = torch.empty(layout.num_slots, heads, DIM, dtype=torch.bfloat16,
-                      device=device)
+        spans = [(8192, (1, 1, 24576), (1, 1, 128))]
+        budget = ('tiles', 32)
+    if spans is None:
+        layout = tiling.identity_layout(real, device)
+    else:
+        layout = tiling.build_tile_layout(
+            [tiling.TiledSpan(st, g, tiling.TileShape(*t))
+             for st, g, t in spans], seq, device)
+    heads = HEADS
+    if cfg == 'cfg1':
+        sets = [make_set(i, range(heads), device) for i in range(2)]
+    else:
+        n_video = layout.n_video_tiles
+        valid = layout.slot_valid.to(torch.bfloat16)[:, None, None]
+        sets = []
+        for i in range(4 if n_layers > 1 else 2):
+            g = torch.Generator(device=device)
+            g.manual_seed(70_001 * i + 17)
+            q, k, v = (torch.randn(layout.num_slots, heads, DIM, generator=g,
+                                   device=device) for _ in range(3))
+            k = k + torch.randn(heads, DIM, generator=g, device=device) * 2.0
+            sets.append({'q': (q.to(torch.bfloat16) * valid).contiguous(),
+                         'k': (k.to(torch.bfloat16) * valid).contiguous(),
+                         'v': (v.to(torch.bfloat16) * valid).contiguous(),
+                         'scores': torch.rand(heads, n_video, n_video,
+                                              generator=g, device=device)})
+    return {'spans': spans, 'seq': seq, 'real': real, 'budget': budget,
+            'n_layers': n_layers, 'full': full_layers, 'sets': sets,
+            'layout': layout, 'heads': heads}
 
-    def layer(i):
-        s = sets[i % n_sets]
-        if i in full_layers:
-            index, count = dense
-        else:
-            index, count = selection.select_index(s['scores'], layout, blocks)
-        quant = ops.quant_pool(s['q'], s['k'], layout.valid_count, 0, pre,
-                               pool=False, out=quant_buf)
-        ops.sparse_attention(quant['q_i8'], quant['q_scale'], quant['k_i8'],
-                             quant['k_scale'], s['v'], index, count,
-                             layout.valid_count, out=out)
-        return count
 
-    pairs = sum(int(layer(i).sum().item()) for i in range(n_layers))
-    ops.check_status(device)
+def _config_line(args, w: dict, ms: float, pairs: int, impl: str) -> dict:
+    """The JSON line of one config run (ms per step, lower is better)."""
+    layout = w['layout']
+    return {'metric': CONFIG_METRICS[args.config].format(seq=w['seq']),
+            'value': ms, 'unit': 'ms', 'impl': impl, 'n_gpus': 1,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
+            'higher_is_better': False, 'scaling': 'none',
+            'vs_baseline': None, 'dtype': 'int8+bf16', 'data': 'synthetic',
+            'config': {'workload': args.config, 'heads': w['heads'],
+                       'seq_len': w['seq'], 'real_tokens': w['real'],
+                       'n_tiles': layout.n_tiles, 'layers': w['n_layers'],
+                       'full_attention_layers': sorted(w['full']),
+                       'kept_pairs_per_step': pairs,
+                       'l2': f"{len(w['sets'])} rotating input sets "
+                             f"(> L2 between reuses)"},
+            'effective_tflops': pairs * OPS_PER_PAIR / (ms * 1e-3) / 1e12}
+
+
+def _time_layers(args, n_layers: int, layer) -> float:
+    """ms per step of `layer(0..n_layers-1)`, CUDA events, after W
+    untimed warm-up steps."""
     for _ in range(args.warmup):
         for i in range(n_layers):
             layer(i)
@@ -438,27 +463,142 @@ def run_config(args, json_out) -> None:
             layer(i)
     end.record()
     torch.cuda.synchronize()
+    return start.elapsed_time(end) / args.steps
+
+
+def run_config(args, json_out) -> None:
+    """BASELINE configs 2-4 on one GPU through this build's kernels (the
+    headline cfg1 line is `main`'s)."""
+    from veda_b200 import kernels, ops, selection
+    device = torch.device('cuda', 0)
+    torch.cuda.set_device(device)
+    w = config_workload(args, device)
+    layout, sets, full = w['layout'], w['sets'], w['full']
+    kind, amount = w['budget']
+    budget = (selection.Budget(tiles=amount) if kind == 'tiles'
+              else selection.Budget.sparsity(amount))
+    blocks = selection.column_blocks(layout, budget,
+                                     selection.Budget(ratio=1.0))
+    dense = selection.dense_index(layout, w['heads'])
+    pre = DIM ** -0.5 * kernels.LOG2E
+    quant_buf = {}
+    out = torch.empty(layout.num_slots, w['heads'], DIM,
+                      dtype=torch.bfloat16, device=device)
+
+    def layer(i):
+        s = sets[i % len(sets)]
+        if i in full:
+            index, count = dense
+        else:
+            index, count = selection.select_index(s['scores'], layout, blocks)
+        quant = ops.quant_pool(s['q'], s['k'], layout.valid_count, 0, pre,
+                               pool=False, out=quant_buf)
+        ops.sparse_attention(quant['q_i8'], quant['q_scale'], quant['k_i8'],
+                             quant['k_scale'], s['v'], index, count,
+                             layout.valid_count, out=out)
+        return count
+
+    pairs = sum(int(layer(i).sum().item()) for i in range(w['n_layers']))
     ops.check_status(device)
-    ms = start.elapsed_time(end) / args.steps
-    tflops = pairs * OPS_PER_PAIR / (ms * 1e-3) / 1e12
-    names = {'cfg2': 'attention time per 48-layer denoising step (ms)',
-             'cfg3': f'sparse-attn call latency (ms) at L={seq}, 90% sparse',
-             'cfg4': 'sparse-attn call latency (ms), 24,576 generated + '
-                     '8,192 global reference tokens'}
-    line = {'metric': names[args.config], 'value': ms, 'unit': 'ms',
-            'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup,
-            'ms_per_step': ms, 'higher_is_better': False,
-            'scaling': 'none', 'vs_baseline': None, 'dtype': 'int8+bf16',
-            'data': 'synthetic',
-            'config': {'workload': args.config, 'heads': heads,
-                       'seq_len': seq, 'real_tokens': real,
-                       'n_tiles': n_tiles, 'layers': n_layers,
-                       'full_attention_layers': sorted(full_layers),
-                       'kept_pairs_per_step': pairs,
-                       'l2': f'{n_sets} rotating input sets '
-                             f'(> L2 between reuses)'},
-            'effective_tflops': tflops,
-            'gpu_launches': 3 * n_layers * args.steps}
+    ms = _time_layers(args, w['n_layers'], layer)
+    ops.check_status(device)
+    line = _config_line(args, w, ms, pairs, 'ours')
+    line['gpu_launches'] = 3 * w['n_layers'] * args.steps
+    print(json.dumps(line), file=json_out, flush=True)
+
+
+REF_PACKAGE = os.path.join(HERE, 'baseline', '_ref')
+
+
+def _reference_gpu_modules():
+    """(selection, tiling, triton_int8) of the unmodified reference package
+    in baseline/_ref, or (None, why not)."""
+    if not os.path.isdir(os.path.join(REF_PACKAGE, 'veda_comfy')):
+        return None, 'the reference package is not in baseline/_ref'
+    if REF_PACKAGE not in sys.path:
+        sys.path.append(REF_PACKAGE)
+    try:
+        from veda_comfy.backends import triton_int8
+        from veda_comfy.core import selection, tiling
+    except Exception as e:  # noqa: BLE001 - reported, not raised
+        return None, f'the reference package does not import: {e}'
+    return (selection, tiling, triton_int8), None
+
+
+def run_reference_gpu(args, rank: int, json_out) -> None:
+    """The reference's own GPU path on one GPU, unmodified, on the inputs,
+    budgets and layer plan `run_config` / `main` time: its torch selection
+    (veda_comfy/core/selection.py `select` and `block_mask`) and its Triton
+    INT8 backend (veda_comfy/backends/triton_int8.py `attend`:
+    `tile_index_list`, then kernels/sage/sparse_int8.py `attend`, which
+    quantises Q and K and runs the block-sparse kernel). Full-attention
+    layers go, as the reference's override sends them
+    (veda_comfy/comfy_patch.py `dense`), to ComfyUI's own attention: torch's
+    scaled_dot_product_attention on [1, H, L, D] views, with ComfyUI's
+    transpose back to [1, L, H*D]. Nothing of this build runs here."""
+    if rank != 0:
+        return
+    mods, why = _reference_gpu_modules()
+    if mods is None:
+        print(json.dumps({'impl': 'reference-triton', 'unavailable': why}),
+              file=json_out, flush=True)
+        return
+    rsel, rtil, rtri = mods
+    device = torch.device('cuda', 0)
+    torch.cuda.set_device(device)
+    w = config_workload(args, device)
+    if w['spans'] is None:
+        spans = [rtil.TiledSpan(0, (1, 1, w['real']),
+                                rtil.TileShape(1, 1, 128))]
+        seq_len = w['real']
+    else:
+        spans = [rtil.TiledSpan(st, g, rtil.TileShape(*t))
+                 for st, g, t in w['spans']]
+        seq_len = w['seq']
+    layout = rtil.build_tile_layout(spans, seq_len, device)
+    kind, amount = w['budget']
+    budget = (rsel.Budget(tiles=amount) if kind == 'tiles'
+              else rsel.Budget.sparsity(amount))
+    blocks = rsel.column_blocks(layout, budget, rsel.Budget(ratio=1.0))
+    backend = rtri.TritonInt8Backend('CUDA')
+    sets, full, real = w['sets'], w['full'], w['real']
+    heads = w['heads']
+
+    def layer(i):
+        s = sets[i % len(sets)]
+        if i in full:
+            q, k, v = (t[:real].permute(1, 0, 2).unsqueeze(0)
+                       for t in (s['q'], s['k'], s['v']))
+            o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+            o.transpose(1, 2).reshape(1, real, heads * DIM)
+            return None
+        index, keep = rsel.select(s['scores'], layout, blocks)
+        mask = rsel.block_mask(index, keep, layout)
+        backend.attend(s['q'], s['k'], s['v'], mask, layout)
+        return mask
+
+    pairs = 0
+    for i in range(w['n_layers']):
+        mask = layer(i)
+        if mask is None:  # every non-empty key tile of every query tile
+            n_ok = int(layout.kv_ok.sum())
+            pairs += heads * n_ok * n_ok
+        else:
+            pairs += int((mask & layout.kv_ok[None, None, :]
+                          & layout.kv_ok[None, :, None]).sum())
+    ms = _time_layers(args, w['n_layers'], layer)
+    line = _config_line(args, w, ms, pairs, 'reference-triton')
+    line['dtype'] = 'int8+fp16'
+    import triton
+    line['reference'] = (
+        'veda_comfy 0.3.1 from baseline/_ref, unmodified: core.selection '
+        f'select + block_mask, backends.triton_int8 attend (Triton '
+        f'{triton.__version__})' + ('; full layers: torch SDPA' if full
+                                    else ''))
+    if args.config == 'cfg1':
+        line.update({'metric': METRIC, 'value': line['effective_tflops'],
+                     'unit': 'TFLOPS', 'higher_is_better': True,
+                     'scaling': 'strong'})
     print(json.dumps(line), file=json_out, flush=True)
 
 
@@ -483,6 +623,9 @@ def main():
         return
     if args.warmup < 3:
         raise SystemExit('--warmup must be at least 3')
+    if args.impl == 'reference-triton':
+        run_reference_gpu(args, rank, json_out)
+        return
     if args.config != 'cfg1':
         if world > 1:
             raise SystemExit('--config cfg2-4 run on one GPU')
