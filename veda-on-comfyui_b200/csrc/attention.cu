@@ -24,7 +24,9 @@
 //                running max with lazy rescaling of O (only when the max
 //                grows by > 2^8), exp2, write P as packed 16-bit pairs over
 //                the first 64 columns of S; at the end of a tile's walk,
-//                normalise O and store the rows.
+//                read O out of TMEM (releasing it for the next walk at
+//                once), normalise it and hand it to the TMA in 32 x 32
+//                boxes through a per-warp staging buffer.
 // TMEM: S_A [0, 128), S_B [128, 256), O_A [256, 384), O_B [384, 512); P
 // aliases S. One thread issues every MMA and the tensor pipe runs them in
 // order, so a Q K^T cannot overwrite P before the P V that reads it, and a
@@ -46,9 +48,9 @@ constexpr uint32_t kVBytes = kTile * kDim * 2;  // 16-bit V tile
 constexpr uint32_t kSmemQ = 0;                  // [slot][buffer] Q tiles
 constexpr uint32_t kSmemK = kSmemQ + 4 * kQBytes;
 constexpr uint32_t kSmemV = kSmemK + kStages * kKBytes;
-// Per softmax warp, 32 rows x 64 bytes: output rows pass through here on
-// their way to a multicast address, so each store moves whole 64-byte row
-// pieces instead of one 16-byte piece per row.
+// Per softmax warp, 32 rows x 64 bytes: output rows pass through here as
+// 32 x 32 boxes, to one asynchronous TMA store (local output) or to
+// multicast stores of whole 64-byte row pieces (head-sharded output).
 constexpr uint32_t kStageBytes = 32 * 64;
 constexpr uint32_t kSmemStage = kSmemV + kStages * kVBytes;
 constexpr uint32_t kSmemBar = kSmemStage + 8 * kStageBytes;
@@ -353,12 +355,16 @@ __device__ __forceinline__ void store_multicast(void* mc, uint4 u) {
       : "memory");
 }
 
-// Columns [32 cc, 32 cc + 32) of the warp's 32 rows (v: this lane's row)
-// through the multicast address: staged in shared memory, then written as
-// eight 64-byte row pieces per instruction. mc0 is the warp's first row.
-template <typename VT>
-__device__ void store_rows_multicast(uint8_t* stage, VT* mc0, int64_t row_sn,
-                                     int cc, int lane, const float* v) {
+// Columns [32 cc, 32 cc + 32) of the warp's 32 rows (v: this lane's row),
+// staged in shared memory. Locally they leave as one asynchronous TMA store
+// of the 32 x 32 box (rows row0 .. row0 + 31 of head `head`); the warp
+// waits only until the TMA has read the staging buffer, not for the global
+// write. Through the multicast address they are written as eight 64-byte
+// row pieces per instruction (mc0: the warp's first row).
+template <typename VT, bool kMulticast>
+__device__ void store_rows(uint8_t* stage, const CUtensorMap* o_map, int head,
+                           int row0, VT* mc0, int64_t row_sn, int cc,
+                           int lane, const float* v) {
   uint4* mine = reinterpret_cast<uint4*>(stage + lane * 64);
 #pragma unroll
   for (int c = 0; c < 32; c += 8) {
@@ -369,28 +375,25 @@ __device__ void store_rows_multicast(uint8_t* stage, VT* mc0, int64_t row_sn,
     u.w = Pack<VT>::two(v[c + 6], v[c + 7]);
     mine[c / 8] = u;
   }
-  __syncwarp();
+  if (kMulticast) {
+    __syncwarp();
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = 8 * i + (lane >> 2), piece = lane & 3;
-    const uint4 u = *reinterpret_cast<const uint4*>(stage + r * 64 + piece * 16);
-    store_multicast(mc0 + r * row_sn + 32 * cc + 8 * piece, u);
+    for (int i = 0; i < 4; ++i) {
+      const int r = 8 * i + (lane >> 2), piece = lane & 3;
+      const uint4 u =
+          *reinterpret_cast<const uint4*>(stage + r * 64 + piece * 16);
+      store_multicast(mc0 + r * row_sn + 32 * cc + 8 * piece, u);
+    }
+  } else {
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(o_map, stage, 32 * cc, head, row0);
+      bulk_commit();
+      bulk_wait_read();
+    }
   }
   __syncwarp();
-}
-
-// 32 outputs of a row, to local memory.
-template <typename VT>
-__device__ void store_row(VT* dst, const float* v) {
-#pragma unroll
-  for (int c = 0; c < 32; c += 8) {
-    uint4 u;
-    u.x = Pack<VT>::two(v[c], v[c + 1]);
-    u.y = Pack<VT>::two(v[c + 2], v[c + 3]);
-    u.z = Pack<VT>::two(v[c + 4], v[c + 5]);
-    u.w = Pack<VT>::two(v[c + 6], v[c + 7]);
-    *reinterpret_cast<uint4*>(dst + c) = u;
-  }
 }
 
 // Per-tile constants of the softmax: the two K-half scales folded with the
@@ -411,11 +414,12 @@ struct TileMeta {
 // INT8 quantisation itself puts into S.
 constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr uint32_t kMaskBits = 0xFF800000u - kMagicBits;
 
 template <typename VT>
 __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
-                             uint32_t tmem, const AttnParams& p, int warp,
-                             int lane) {
+                             uint32_t tmem, const AttnParams& p,
+                             const CUtensorMap* o_map, int warp, int lane) {
   volatile int* abort = &b.abort;
   uint8_t* stage = smem + kSmemStage + (warp - 4) * kStageBytes;
   const int quarter = warp & 3;  // TMEM lanes this warp may access
@@ -433,23 +437,24 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
     const int head = pr.head;
     const int64_t out_off = static_cast<int64_t>(qt * kTile + row) * p.out_sn +
                             static_cast<int64_t>(head) * p.out_sh;
-    VT* out = static_cast<VT*>(p.out) + out_off;
-    VT* out_mc = p.out_mc != nullptr ? static_cast<VT*>(p.out_mc) + out_off
-                                     : nullptr;
-    // the warp's first row through the multicast address
-    VT* mc0 = out_mc != nullptr ? out_mc - lane * p.out_sn : nullptr;
+    // the warp's first row (the output map's row coordinate) and its
+    // multicast address
+    const int row0 = qt * kTile + quarter * 32;
+    VT* mc0 = p.out_mc != nullptr
+                  ? static_cast<VT*>(p.out_mc) + out_off - lane * p.out_sn
+                  : nullptr;
     if (count == 0) {  // nothing kept: the reference's acc / 1 = 0
-      if (mc0 != nullptr) {
-        float zero[32];
+      float zero[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) zero[c] = 0.0f;
+      for (int c = 0; c < 32; ++c) zero[c] = 0.0f;
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc)
-          store_rows_multicast<VT>(stage, mc0, p.out_sn, cc, lane, zero);
-      } else {
-#pragma unroll
-        for (int c = 0; c < kDim; c += 8)
-          *reinterpret_cast<uint4*>(out + c) = make_uint4(0, 0, 0, 0);
+      for (int cc = 0; cc < 4; ++cc) {
+        if (mc0 != nullptr)
+          store_rows<VT, true>(stage, o_map, head, row0, mc0, p.out_sn, cc,
+                               lane, zero);
+        else
+          store_rows<VT, false>(stage, o_map, head, row0, mc0, p.out_sn, cc,
+                                lane, zero);
       }
       continue;
     }
@@ -498,26 +503,29 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
       reg_fence32(r + 32);
       reg_fence32(r + 64);
       reg_fence32(r + 96);
-#pragma unroll
-      for (int c = 0; c < 128; ++c) r[c] += kMagicBits;
-      // valid is the tile's (the same in every lane): a warp-uniform branch
+      // valid is the tile's (the same in every lane): a warp-uniform branch.
+      // Masked columns get kMaskBits: never the integer max (every real S
+      // is above -2^21), and -inf once the bias is added.
       if (__any_sync(0xffffffffu, cur.valid < kTile)) {
 #pragma unroll
         for (int c = 0; c < 128; ++c)
-          if (c >= cur.valid) r[c] = 0xFF800000u;  // -inf: never the max, p = 0
+          if (c >= cur.valid) r[c] = kMaskBits;
       }
-      // row max of each 64-column half on the biased values (monotone in S)
-      float ma0 = -INFINITY, mb0 = -INFINITY, ma1 = -INFINITY,
-            mb1 = -INFINITY;
+      // row max of each 64-column half on the raw int32 S (the biased
+      // values are monotone in S, so the bias is added to the two maxima
+      // here and to every value in the exponential pass below)
+      int ia0 = INT_MIN, ib0 = INT_MIN, ia1 = INT_MIN, ib1 = INT_MIN;
 #pragma unroll
-      for (int c = 0; c < 64; c += 4) {
-        ma0 = max3(ma0, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
-        mb0 = max3(mb0, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
-        ma1 = max3(ma1, __uint_as_float(r[c + 64]), __uint_as_float(r[c + 65]));
-        mb1 = max3(mb1, __uint_as_float(r[c + 66]), __uint_as_float(r[c + 67]));
+      for (int c = 0; c < 64; c += 2) {
+        ia0 = max(ia0, static_cast<int>(r[c]));
+        ib0 = max(ib0, static_cast<int>(r[c + 1]));
+        ia1 = max(ia1, static_cast<int>(r[c + 64]));
+        ib1 = max(ib1, static_cast<int>(r[c + 65]));
       }
-      const float mt = fmaxf(fmaf(fmaxf(ma0, mb0), cur.sc0, -cur.off0),
-                             fmaf(fmaxf(ma1, mb1), cur.sc1, -cur.off1));
+      const uint32_t top0 = static_cast<uint32_t>(max(ia0, ib0)) + kMagicBits;
+      const uint32_t top1 = static_cast<uint32_t>(max(ia1, ib1)) + kMagicBits;
+      const float mt = fmaxf(fmaf(__uint_as_float(top0), cur.sc0, -cur.off0),
+                             fmaf(__uint_as_float(top1), cur.sc1, -cur.off1));
       const bool need = mt > m + kRescaleThreshold;
       float alpha = 1.0f;
       if (need) {
@@ -533,7 +541,8 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
         const uint64_t z =
-            fma2(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+            fma2(f2(__uint_as_float(r[2 * i] + kMagicBits),
+                    __uint_as_float(r[2 * i + 1] + kMagicBits)),
                  i < 32 ? s0 : s1, i < 32 ? n0 : n1);
         float z0, z1;
         f2_split(z, z0, z1);
@@ -589,25 +598,36 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
       break;
     }
     tc_fence_after();
-    const float inv = l > 0.0f ? 1.0f / l : 1.0f;
-#pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
-      uint32_t o[32];
-      tmem_ld32(o_addr + 32 * cc, o);
-      tmem_ld_wait(o);
-      float v[32];
-#pragma unroll
-      for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(o[c]) * inv;
-      if (mc0 != nullptr)
-        store_rows_multicast<VT>(stage, mc0, p.out_sn, cc, lane, v);
-      else
-        store_row<VT>(out + 32 * cc, v);
-    }
-    // O of this slot may now be overwritten by the next walk's first P V.
+    // O comes out of TMEM at once, and the slot's O is released before the
+    // stores, so the next walk's first P V does not wait for them.
+    uint32_t o[128];
+    tmem_ld32(o_addr + 0, o);
+    tmem_ld32(o_addr + 32, o + 32);
+    tmem_ld32(o_addr + 64, o + 64);
+    tmem_ld32(o_addr + 96, o + 96);
+    tmem_ld_wait(o);
+    reg_fence32(o + 32);
+    reg_fence32(o + 64);
+    reg_fence32(o + 96);
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&b.o_free[slot]);
+    const float inv = l > 0.0f ? 1.0f / l : 1.0f;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      float v[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(o[32 * cc + c]) * inv;
+      if (mc0 != nullptr)
+        store_rows<VT, true>(stage, o_map, head, row0, mc0, p.out_sn, cc,
+                             lane, v);
+      else
+        store_rows<VT, false>(stage, o_map, head, row0, mc0, p.out_sn, cc,
+                              lane, v);
+    }
   }
+  // The TMA stores have written their rows before the CTA exits.
+  if (lane == 0) bulk_wait();
   // Multicast rows are ordered before whatever the host does next to
   // signal the other GPUs (a collective on the same stream).
   if (p.out_mc != nullptr) __threadfence_system();
@@ -627,6 +647,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     sparse_attention_kernel(const __grid_constant__ CUtensorMap q_map,
                             const __grid_constant__ CUtensorMap k_map,
                             const __grid_constant__ CUtensorMap v_map,
+                            const __grid_constant__ CUtensorMap o_map,
                             const AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   Barriers& b = *reinterpret_cast<Barriers*>(smem + kSmemBar);
@@ -673,7 +694,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     regs_inc<kHighRegs>();
-    if (run) softmax_loop<VT>((warp - 4) >> 2, smem, b, tmem, p, warp, lane);
+    if (run)
+      softmax_loop<VT>((warp - 4) >> 2, smem, b, tmem, p, &o_map, warp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -688,7 +710,8 @@ std::atomic<int> g_sm_count[64];
 
 template <typename VT>
 int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
-           const AttnParams& p, cudaStream_t stream, int dt) {
+           const CUtensorMap& om, const AttnParams& p, cudaStream_t stream,
+           int dt) {
   const int device = current_device();
   int sms = 148;
   if (device >= 0 && device < 64 && g_sm_count[device].load() > 0) {
@@ -706,7 +729,7 @@ int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
   }
   const int grid = p.n_pairs < sms ? p.n_pairs : sms;
   sparse_attention_kernel<VT><<<grid, kAttnThreads, kSmemBytes, stream>>>(
-      qm, km, vm, p);
+      qm, km, vm, om, p);
   VEDA_CHECK_CUDA(cudaGetLastError());
   return VEDA_OK;
 }
@@ -770,6 +793,22 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
             3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
+  // The output as [slot][head][dim], written by TMA in 32 x 32 boxes.
+  CUtensorMap om;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(kDim),
+                              static_cast<uint64_t>(heads),
+                              static_cast<uint64_t>(n_slots)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(out_stride_h) * 2,
+                                 static_cast<uint64_t>(out_stride_n) * 2};
+    const uint32_t box[3] = {32, 1, 32};
+    if (int rc = encode_tiled(
+            &om,
+            v_dtype == VEDA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+            3, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  }
   AttnParams p{};
   p.q_scale = q_scale;
   p.k_scale = k_scale;
@@ -786,8 +825,9 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
   p.n_pairs = heads * ((n_tiles + 1) / 2);
   p.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (v_dtype == VEDA_BF16) return launch<__nv_bfloat16>(qm, km, vm, p, s, 0);
-  return launch<__half>(qm, km, vm, p, s, 1);
+  if (v_dtype == VEDA_BF16)
+    return launch<__nv_bfloat16>(qm, km, vm, om, p, s, 0);
+  return launch<__half>(qm, km, vm, om, p, s, 1);
 }
 
 }  // namespace

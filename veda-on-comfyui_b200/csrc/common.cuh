@@ -120,6 +120,33 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, void* dst,
       : "memory");
 }
 
+// Asynchronous bulk tensor store of a shared-memory box to global memory,
+// tracked by this thread's bulk groups; the source may be rewritten once
+// bulk_wait_read() returns (the global write completes later).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map,
+                                             const void* src, int x, int y,
+                                             int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, "
+      "%4}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) reads of them.
+__device__ __forceinline__ void fence_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, void* dst,
                                             uint64_t* bar, int x, int y,
                                             int z) {
@@ -320,30 +347,6 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
 __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-// Named barrier over `count` threads that also ORs a predicate across them.
-__device__ __forceinline__ bool bar_any(uint32_t id, uint32_t count, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
-
-__device__ __forceinline__ void bar_sync(uint32_t id, uint32_t count) {
-  asm volatile("barrier.sync.aligned %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
 
