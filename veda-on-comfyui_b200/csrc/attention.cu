@@ -19,6 +19,10 @@
 //                O(TMEM, f32) += P(TMEM) V(smem) as 8 x kind::f16 (K = 16).
 //                While one slot's softmax runs, the tensor core serves the
 //                other slot, so exp and MMA overlap.
+//   warps 2-3    head-sharded output only: the pushers of slots A and B.
+//                They read each finished walk's rows back from this GPU's
+//                copy and write them through the NVSwitch multicast
+//                address while later walks compute.
 //   warps 4-7    softmax of slot A, warps 8-11 of slot B: one query row per
 //                thread (TMEM lane = row); load the S row, scale, mask,
 //                running max with lazy rescaling of O (only when the max
@@ -49,8 +53,7 @@ constexpr uint32_t kSmemQ = 0;                  // [slot][buffer] Q tiles
 constexpr uint32_t kSmemK = kSmemQ + 4 * kQBytes;
 constexpr uint32_t kSmemV = kSmemK + kStages * kKBytes;
 // Per softmax warp, 32 rows x 64 bytes: output rows pass through here as
-// 32 x 32 boxes, to one asynchronous TMA store (local output) or to
-// multicast stores of whole 64-byte row pieces (head-sharded output).
+// 32 x 32 boxes on their way to one asynchronous TMA store each.
 constexpr uint32_t kStageBytes = 32 * 64;
 constexpr uint32_t kSmemStage = kSmemV + kStages * kVBytes;
 constexpr uint32_t kSmemBar = kSmemStage + 8 * kStageBytes;
@@ -84,6 +87,9 @@ struct Barriers {
   uint64_t fin;
   uint32_t tmem_base;
   int abort;
+  // Head-sharded output: walks whose rows of each (slot, TMEM quarter) are
+  // complete in this GPU's copy, for the pusher warps.
+  int published[kSlots][4];
 };
 static_assert(sizeof(Barriers) <= 512, "barrier block too large");
 
@@ -356,15 +362,12 @@ __device__ __forceinline__ void store_multicast(void* mc, uint4 u) {
 }
 
 // Columns [32 cc, 32 cc + 32) of the warp's 32 rows (v: this lane's row),
-// staged in shared memory. Locally they leave as one asynchronous TMA store
-// of the 32 x 32 box (rows row0 .. row0 + 31 of head `head`); the warp
-// waits only until the TMA has read the staging buffer, not for the global
-// write. Through the multicast address they are written as eight 64-byte
-// row pieces per instruction (mc0: the warp's first row).
-template <typename VT, bool kMulticast>
+// staged in shared memory and written as one asynchronous TMA store of the
+// 32 x 32 box (rows row0 .. row0 + 31 of head `head`); the warp waits only
+// until the TMA has read the staging buffer, not for the global write.
+template <typename VT>
 __device__ void store_rows(uint8_t* stage, const CUtensorMap* o_map, int head,
-                           int row0, VT* mc0, int64_t row_sn, int cc,
-                           int lane, const float* v) {
+                           int row0, int cc, int lane, const float* v) {
   uint4* mine = reinterpret_cast<uint4*>(stage + lane * 64);
 #pragma unroll
   for (int c = 0; c < 32; c += 8) {
@@ -375,23 +378,12 @@ __device__ void store_rows(uint8_t* stage, const CUtensorMap* o_map, int head,
     u.w = Pack<VT>::two(v[c + 6], v[c + 7]);
     mine[c / 8] = u;
   }
-  if (kMulticast) {
-    __syncwarp();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = 8 * i + (lane >> 2), piece = lane & 3;
-      const uint4 u =
-          *reinterpret_cast<const uint4*>(stage + r * 64 + piece * 16);
-      store_multicast(mc0 + r * row_sn + 32 * cc + 8 * piece, u);
-    }
-  } else {
-    fence_async_shared();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_3d(o_map, stage, 32 * cc, head, row0);
-      bulk_commit();
-      bulk_wait_read();
-    }
+  fence_async_shared();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(o_map, stage, 32 * cc, head, row0);
+    bulk_commit();
+    bulk_wait_read();
   }
   __syncwarp();
 }
@@ -416,6 +408,83 @@ constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
 constexpr uint32_t kMaskBits = 0xFF800000u - kMagicBits;
 
+// Waits (bounded) until more than `walks` walks are published.
+__device__ __forceinline__ bool wait_published(const int* counter, int walks,
+                                               volatile int* abort,
+                                               int32_t* status) {
+  const volatile int* n = counter;
+  if (*n <= walks) {
+    const uint64_t start = global_ns();
+    while (*n <= walks) {
+      if (*abort) return false;
+      if (global_ns() - start > kWaitLimitNs) {
+        *abort = 1;
+        report(status, VEDA_STATUS_TIMEOUT);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  __threadfence_block();  // the rows published before the count
+  return true;
+}
+
+// 16 bytes from global memory through L2 only (rows this CTA's TMA stores
+// just wrote; nothing of them sits in L1).
+__device__ __forceinline__ uint4 ld_cg_v4(const void* ptr) {
+  uint4 u;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+               : "l"(ptr));
+  return u;
+}
+
+// Warps 2 and 3, head-sharded output only: the pusher of slot s. The
+// softmax warps write their rows to this GPU's copy of the output (TMA
+// stores) and publish each walk per TMEM quarter; the pusher reads the
+// published rows back (from L2) and writes them through the multicast
+// address, so NVSwitch delivers them to every GPU while the next walks
+// compute. Rows are never rewritten within a launch, so the pusher may lag.
+template <typename VT>
+__device__ void push_slot(int s, Barriers& b, const AttnParams& p, int lane) {
+  volatile int* abort = &b.abort;
+  const char* local = static_cast<const char*>(p.out);
+  char* mc = static_cast<char*>(p.out_mc);
+  const int64_t row_bytes = p.out_sn * static_cast<int64_t>(sizeof(VT));
+  const int64_t head_bytes = p.out_sh * static_cast<int64_t>(sizeof(VT));
+  int walks = 0;
+  bool ok = true;
+  for (int w = blockIdx.x; ok && w < p.n_pairs; w += gridDim.x) {
+    const Pair pr = decode_pair(w, p);
+    const int qt = pr.qt[s];
+    if (qt >= p.n_tiles) continue;
+    for (int q = 0; q < 4 && ok; ++q) {
+      ok = wait_published(&b.published[s][q], walks, abort, p.status);
+      if (!ok) break;
+      // 32 rows x 256 bytes: lane l moves bytes 16 (l % 16) of rows
+      // l / 16, l / 16 + 2, ..., four loads in flight.
+      const int64_t first = static_cast<int64_t>(qt * kTile + q * 32 +
+                                                 (lane >> 4)) * row_bytes +
+                            pr.head * head_bytes + 16 * (lane & 15);
+      const int64_t step = 2 * row_bytes;
+#pragma unroll
+      for (int k0 = 0; k0 < 16; k0 += 4) {
+        uint4 u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          u[k] = ld_cg_v4(local + first + (k0 + k) * step);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          store_multicast(mc + first + (k0 + k) * step, u[k]);
+      }
+    }
+    ++walks;
+  }
+  // Multicast rows are ordered before whatever the host does next to
+  // signal the other GPUs (a collective on the same stream).
+  __threadfence_system();
+}
+
 template <typename VT>
 __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
                              uint32_t tmem, const AttnParams& p,
@@ -429,33 +498,40 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
   const uint32_t o_addr = lane_addr + tmem_o(slot);
   int tiles = 0, items = 0;  // phases of s_full / o_ready of this slot
   bool good = true;
+  // Head-sharded output: a walk's rows are published to the pusher warp
+  // once their TMA stores have completed. That wait is put off until the
+  // next walk's first S, a pair this slot has no work in, or the end.
+  const bool sharded = p.out_mc != nullptr;
+  bool unpublished = false;
+  auto publish = [&]() {
+    if (!unpublished) return;
+    if (lane == 0) {
+      bulk_wait();
+      fence_async_global();
+      __threadfence_block();
+      volatile int* n = &b.published[slot][quarter];
+      *n = *n + 1;
+    }
+    __syncwarp();
+    unpublished = false;
+  };
   for (int w = blockIdx.x; good && w < p.n_pairs; w += gridDim.x) {
     const Pair pr = decode_pair(w, p);
     const int qt = pr.qt[slot];
     if (qt >= p.n_tiles) continue;
     const int count = pr.count[slot];
     const int head = pr.head;
-    const int64_t out_off = static_cast<int64_t>(qt * kTile + row) * p.out_sn +
-                            static_cast<int64_t>(head) * p.out_sh;
-    // the warp's first row (the output map's row coordinate) and its
-    // multicast address
+    // the warp's first row: the output map's row coordinate
     const int row0 = qt * kTile + quarter * 32;
-    VT* mc0 = p.out_mc != nullptr
-                  ? static_cast<VT*>(p.out_mc) + out_off - lane * p.out_sn
-                  : nullptr;
     if (count == 0) {  // nothing kept: the reference's acc / 1 = 0
+      publish();
       float zero[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) zero[c] = 0.0f;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        if (mc0 != nullptr)
-          store_rows<VT, true>(stage, o_map, head, row0, mc0, p.out_sn, cc,
-                               lane, zero);
-        else
-          store_rows<VT, false>(stage, o_map, head, row0, mc0, p.out_sn, cc,
-                                lane, zero);
-      }
+      for (int cc = 0; cc < 4; ++cc)
+        store_rows<VT>(stage, o_map, head, row0, cc, lane, zero);
+      unpublished = sharded;
       continue;
     }
     const int32_t* idx = pr.idx[slot];
@@ -493,6 +569,7 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
         good = false;
         break;
       }
+      if (j == 0) publish();
       tc_fence_after();
       uint32_t r[128];
       tmem_ld32(s_addr + 0, r);
@@ -618,19 +695,13 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
       float v[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(o[32 * cc + c]) * inv;
-      if (mc0 != nullptr)
-        store_rows<VT, true>(stage, o_map, head, row0, mc0, p.out_sn, cc,
-                             lane, v);
-      else
-        store_rows<VT, false>(stage, o_map, head, row0, mc0, p.out_sn, cc,
-                              lane, v);
+      store_rows<VT>(stage, o_map, head, row0, cc, lane, v);
     }
+    unpublished = sharded;
   }
+  if (good) publish();
   // The TMA stores have written their rows before the CTA exits.
   if (lane == 0) bulk_wait();
-  // Multicast rows are ordered before whatever the host does next to
-  // signal the other GPUs (a collective on the same stream).
-  if (p.out_mc != nullptr) __threadfence_system();
 }
 
 template <uint32_t N>
@@ -674,6 +745,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&b.v_empty[st], 1);
     }
     mbar_init(&b.fin, 1);
+    for (int s = 0; s < kSlots; ++s)
+      for (int q = 0; q < 4; ++q) b.published[s][q] = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(&b.tmem_base, kTmemCols);
@@ -691,6 +764,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     } else if (run && warp == 1) {
       if (lane == 0) issue_mma<VT>(smem, b, tmem, p);
       __syncwarp();
+    } else if (run && warp >= 2 && p.out_mc != nullptr) {
+      push_slot<VT>(warp - 2, b, p, lane);
     }
   } else {
     regs_inc<kHighRegs>();

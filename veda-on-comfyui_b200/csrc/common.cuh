@@ -144,6 +144,11 @@ __device__ __forceinline__ void bulk_wait_read() {
 __device__ __forceinline__ void bulk_wait() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+// Orders this thread's completed async-proxy (TMA) global writes before its
+// later generic-proxy accesses, so a release that follows publishes them.
+__device__ __forceinline__ void fence_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA) reads of them.
 __device__ __forceinline__ void fence_async_shared() {
