@@ -190,14 +190,16 @@ int veda_sparse_attention(const int8_t* q_i8, const float* q_scale,
                           int32_t* status, void* stream);
 
 /*
- * veda_sparse_attention for head-sharded runs: every output row is stored
- * once through `out_multicast`, the NVSwitch multicast address of `out`
- * (the same byte offsets), so each GPU bound to the multicast object ends
- * up holding every rank's heads. This replaces the all-gather of the
- * output that head sharding needs (no counterpart in the reference, which
- * runs on one GPU). The caller orders the stores before reading other
- * ranks' heads with a collective on the same stream (the kernel ends with
- * a system-scope fence). `out` is still this rank's buffer.
+ * veda_sparse_attention for head-sharded runs: every output row is written
+ * to `out` and then, while later rows are still being computed, once
+ * through `out_multicast`, the NVSwitch multicast address of `out` (the
+ * same byte offsets), so each GPU bound to the multicast object ends up
+ * holding every rank's heads. This replaces the all-gather of the output
+ * that head sharding needs (no counterpart in the reference, which runs on
+ * one GPU). The caller orders the stores before reading other ranks' heads
+ * with a collective on the same stream (the kernel ends with a
+ * system-scope fence). `out` is this rank's view of the multicast-bound
+ * buffer.
  */
 int veda_sparse_attention_multicast(
     const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,

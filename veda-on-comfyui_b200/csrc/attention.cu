@@ -492,7 +492,6 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
   volatile int* abort = &b.abort;
   uint8_t* stage = smem + kSmemStage + (warp - 4) * kStageBytes;
   const int quarter = warp & 3;  // TMEM lanes this warp may access
-  const int row = quarter * 32 + lane;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
   const uint32_t s_addr = lane_addr + tmem_s(slot);
   const uint32_t o_addr = lane_addr + tmem_o(slot);
