@@ -527,6 +527,19 @@ def _reference_gpu_modules():
     return (selection, tiling, triton_int8), None
 
 
+def reference_layout(rtil, spans, seq: int, real: int, device):
+    """The reference's own TileLayout (core/tiling.py build_tile_layout) of
+    a config: `spans` as in `config_workload` (None: rows already in tile
+    order, one 1 x 1 x L span of `real` rows)."""
+    if spans is None:
+        return rtil.build_tile_layout(
+            [rtil.TiledSpan(0, (1, 1, real), rtil.TileShape(1, 1, 128))],
+            real, device)
+    return rtil.build_tile_layout(
+        [rtil.TiledSpan(st, g, rtil.TileShape(*t)) for st, g, t in spans],
+        seq, device)
+
+
 def run_reference_gpu(args, rank: int, json_out) -> None:
     """The reference's own GPU path on one GPU, unmodified, on the inputs,
     budgets and layer plan `run_config` / `main` time: its torch selection
@@ -549,15 +562,7 @@ def run_reference_gpu(args, rank: int, json_out) -> None:
     device = torch.device('cuda', 0)
     torch.cuda.set_device(device)
     w = config_workload(args, device)
-    if w['spans'] is None:
-        spans = [rtil.TiledSpan(0, (1, 1, w['real']),
-                                rtil.TileShape(1, 1, 128))]
-        seq_len = w['real']
-    else:
-        spans = [rtil.TiledSpan(st, g, rtil.TileShape(*t))
-                 for st, g, t in w['spans']]
-        seq_len = w['seq']
-    layout = rtil.build_tile_layout(spans, seq_len, device)
+    layout = reference_layout(rtil, w['spans'], w['seq'], w['real'], device)
     kind, amount = w['budget']
     budget = (rsel.Budget(tiles=amount) if kind == 'tiles'
               else rsel.Budget.sparsity(amount))
