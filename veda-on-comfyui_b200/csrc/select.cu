@@ -86,7 +86,10 @@ __device__ void emit_topk(Emitter& em, const SelectParams& p,
   const int n_cols = stop - start;
   uint32_t thresh = 0;
   if (kk < n_cols) {
-    // Largest T with |{key >= T}| >= kk: the kk-th largest key.
+    // Largest T with |{key >= T}| >= kk: the kk-th largest key. The search
+    // stops early once exactly kk keys are >= T: those are the kk largest,
+    // and the selection below (every key > T, then keys == T) keeps exactly
+    // them, as it would with the exact kk-th largest key.
 #pragma unroll 1
     for (int bit = 31; bit >= 0; --bit) {
       const uint32_t cand = thresh | (1u << bit);
@@ -96,6 +99,7 @@ __device__ void emit_topk(Emitter& em, const SelectParams& p,
         cnt += (start + 32 * i + lane < stop && key[i] >= cand) ? 1 : 0;
       cnt = __reduce_add_sync(kFull, cnt);
       if (cnt >= kk) thresh = cand;
+      if (cnt == kk) break;  // warp-uniform
     }
   }
   int above = 0;
