@@ -210,6 +210,35 @@ int veda_sparse_attention_multicast(
     int32_t* status, void* stream);
 
 /*
+ * veda_quant_pool on packed rows: q and k are [seq_len, heads, 128] in
+ * sequence order and slot i of the tile order reads row perm[i] (< 0:
+ * padding, zeros), so the gather of core/tiling.py:227-242 (gather_tiles)
+ * happens in the same read. Outputs as veda_quant_pool, same bits as
+ * veda_gather_tiles followed by veda_quant_pool. perm has n_slots entries.
+ */
+int veda_quant_pool_packed(
+    const void* q, const void* k, int dtype, int64_t stride_n,
+    int64_t stride_h, int64_t seq_len, const int64_t* perm, int n_slots,
+    int heads, const int32_t* valid_count, int n_video_tiles,
+    float q_pre_scale, int8_t* q_i8, float* q_scale, int8_t* k_i8,
+    float* k_scale, float* feats_q, float* feats_k, void* stream);
+
+/*
+ * veda_sparse_attention with a packed output: row `slot` of the result goes
+ * to row perm[slot] of `out` ([seq_len, heads, 128], any row and head
+ * strides), padding slots (perm < 0) are dropped, so the scatter of
+ * core/tiling.py:245-252 (scatter_tiles_) happens in the kernel's epilogue.
+ * Same bits as veda_sparse_attention followed by veda_scatter_tiles.
+ */
+int veda_sparse_attention_packed(
+    const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
+    const float* k_scale, const void* v, int v_dtype, int64_t v_stride_n,
+    int64_t v_stride_h, const int32_t* index, int width, const int32_t* count,
+    const int32_t* valid_count, int heads, int n_tiles, void* out,
+    int64_t out_stride_n, int64_t out_stride_h, const int64_t* perm,
+    int64_t seq_len, int32_t* status, void* stream);
+
+/*
  * Tile-order permutation of packed rows (core/tiling.py:227-242,
  * gather_tiles): out[slot, j, :] = x[perm[slot], heads[j], :], and zero
  * where perm[slot] < 0. x is [seq_len, total_heads, 128] 16-bit with

@@ -102,6 +102,10 @@ struct AttnParams {
   void* out;
   void* out_mc;          // multicast address of out (element 0), or null
   int64_t out_sn, out_sh;
+  // Packed output (null: tile order): slot -> row of `out`, < 0 for
+  // padding, which is dropped (core/tiling.py:245-252).
+  const int64_t* perm;
+  int64_t seq_len;
   int n_tiles, width, heads;
   int n_pairs;           // heads * ceil(n_tiles / 2)
   int32_t* status;
@@ -388,6 +392,38 @@ __device__ void store_rows(uint8_t* stage, const CUtensorMap* o_map, int head,
   __syncwarp();
 }
 
+// The same box through the packed-output permutation: the staged rows leave
+// as 64-byte pieces, eight rows per instruction, each to row perm[slot] of
+// `out` (dst: element 0 of `out` plus the head offset), padding dropped.
+// dest[i] is the destination row of row 8 i + lane / 4 of the warp's 32.
+template <typename VT>
+__device__ void store_rows_packed(uint8_t* stage, VT* dst, int64_t row_sn,
+                                  const int64_t* dest, int cc, int lane,
+                                  const float* v) {
+  uint4* mine = reinterpret_cast<uint4*>(stage + lane * 64);
+#pragma unroll
+  for (int c = 0; c < 32; c += 8) {
+    uint4 u;
+    u.x = Pack<VT>::two(v[c], v[c + 1]);
+    u.y = Pack<VT>::two(v[c + 2], v[c + 3]);
+    u.z = Pack<VT>::two(v[c + 4], v[c + 5]);
+    u.w = Pack<VT>::two(v[c + 6], v[c + 7]);
+    mine[c / 8] = u;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 8 * i + (lane >> 2), piece = lane & 3;
+    if (dest[i] >= 0) {
+      const uint4 u =
+          *reinterpret_cast<const uint4*>(stage + r * 64 + piece * 16);
+      *reinterpret_cast<uint4*>(dst + dest[i] * row_sn + 32 * cc +
+                                8 * piece) = u;
+    }
+  }
+  __syncwarp();
+}
+
 // Per-tile constants of the softmax: the two K-half scales folded with the
 // Q scale, the magic-number offsets that go with them, the valid rows. The
 // global loads behind them (K scales, valid count, next tile id) are issued
@@ -522,6 +558,16 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
     const int head = pr.head;
     // the warp's first row: the output map's row coordinate
     const int row0 = qt * kTile + quarter * 32;
+    // packed output: the destination rows of this lane's four row pieces
+    int64_t dest[4] = {-1, -1, -1, -1};
+    if (p.perm != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t d = __ldg(p.perm + row0 + 8 * i + (lane >> 2));
+        dest[i] = d < p.seq_len ? d : -1;
+      }
+    }
+    VT* packed = static_cast<VT*>(p.out) + static_cast<int64_t>(head) * p.out_sh;
     if (count == 0) {  // nothing kept: the reference's acc / 1 = 0
       publish();
       float zero[32];
@@ -529,7 +575,10 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
       for (int c = 0; c < 32; ++c) zero[c] = 0.0f;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc)
-        store_rows<VT>(stage, o_map, head, row0, cc, lane, zero);
+        if (p.perm != nullptr)
+          store_rows_packed<VT>(stage, packed, p.out_sn, dest, cc, lane, zero);
+        else
+          store_rows<VT>(stage, o_map, head, row0, cc, lane, zero);
       unpublished = sharded;
       continue;
     }
@@ -694,7 +743,10 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
       float v[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(o[32 * cc + c]) * inv;
-      store_rows<VT>(stage, o_map, head, row0, cc, lane, v);
+      if (p.perm != nullptr)
+        store_rows_packed<VT>(stage, packed, p.out_sn, dest, cc, lane, v);
+      else
+        store_rows<VT>(stage, o_map, head, row0, cc, lane, v);
     }
     unpublished = sharded;
   }
@@ -821,8 +873,11 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
            int width, const int32_t* count, const int32_t* valid_count,
            int heads, int n_tiles, void* out, void* out_mc,
            int64_t out_stride_n, int64_t out_stride_h, int32_t* status,
-           void* stream) {
+           void* stream, const int64_t* perm = nullptr, int64_t seq_len = 0) {
   if (int rc = check_device()) return rc;
+  if (perm != nullptr && (seq_len <= 0 || out_mc != nullptr))
+    return fail(VEDA_ERR_INVALID,
+                "packed output needs seq_len > 0 and no multicast address");
   if (heads <= 0 || heads > 65535 || n_tiles <= 0 || width <= 0)
     return fail(VEDA_ERR_INVALID, "bad sizes: heads %d, n_tiles %d, width %d",
                 heads, n_tiles, width);
@@ -870,9 +925,11 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
   // The output as [slot][head][dim], written by TMA in 32 x 32 boxes.
   CUtensorMap om;
   {
-    const uint64_t dims[3] = {static_cast<uint64_t>(kDim),
-                              static_cast<uint64_t>(heads),
-                              static_cast<uint64_t>(n_slots)};
+    // (over the packed rows when the output is packed: the map is then
+    // not used, and must not reach past them)
+    const uint64_t dims[3] = {
+        static_cast<uint64_t>(kDim), static_cast<uint64_t>(heads),
+        static_cast<uint64_t>(perm != nullptr ? seq_len : n_slots)};
     const uint64_t strides[2] = {static_cast<uint64_t>(out_stride_h) * 2,
                                  static_cast<uint64_t>(out_stride_n) * 2};
     const uint32_t box[3] = {32, 1, 32};
@@ -893,6 +950,8 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
   p.out_mc = out_mc;
   p.out_sn = out_stride_n;
   p.out_sh = out_stride_h;
+  p.perm = perm;
+  p.seq_len = seq_len;
   p.n_tiles = n_tiles;
   p.width = width;
   p.heads = heads;
@@ -932,4 +991,18 @@ extern "C" int veda_sparse_attention_multicast(
                 v_stride_h, index, width, count, valid_count, heads, n_tiles,
                 out, out_multicast, out_stride_n, out_stride_h, status,
                 stream);
+}
+
+extern "C" int veda_sparse_attention_packed(
+    const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
+    const float* k_scale, const void* v, int v_dtype, int64_t v_stride_n,
+    int64_t v_stride_h, const int32_t* index, int width, const int32_t* count,
+    const int32_t* valid_count, int heads, int n_tiles, void* out,
+    int64_t out_stride_n, int64_t out_stride_h, const int64_t* perm,
+    int64_t seq_len, int32_t* status, void* stream) {
+  if (perm == nullptr) return fail(VEDA_ERR_INVALID, "null perm");
+  return attend(q_i8, q_scale, k_i8, k_scale, v, v_dtype, v_stride_n,
+                v_stride_h, index, width, count, valid_count, heads, n_tiles,
+                out, nullptr, out_stride_n, out_stride_h, status, stream, perm,
+                seq_len);
 }

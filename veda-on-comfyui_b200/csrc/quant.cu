@@ -34,6 +34,10 @@ struct QuantParams {
   int n_tiles;
   const int32_t* valid;        // [n_tiles] or null (all 128)
   int n_video;
+  // Packed input (null: rows already in tile order): slot -> packed row,
+  // < 0 for padding, which reads as zeros (core/tiling.py:227-242).
+  const int64_t* perm;
+  int64_t seq_len;
 };
 
 // Eight 16-bit values of one 16-byte load, widened to fp32 (exact).
@@ -88,12 +92,16 @@ __global__ void __launch_bounds__(kQuantThreads, POOL ? 2 : 3)
   const int rg = tid >> 4;  // rows rg + 16 i
 
   const T* x = static_cast<const T*>(job.x) +
-               static_cast<int64_t>(tile) * kTile * p.stride_n +
                static_cast<int64_t>(head) * p.stride_h + 8 * dc;
   uint4 raw[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-    raw[i] = __ldg(reinterpret_cast<const uint4*>(x + (rg + 16 * i) * p.stride_n));
+  for (int i = 0; i < 8; ++i) {
+    int64_t row = static_cast<int64_t>(tile) * kTile + rg + 16 * i;
+    if (p.perm != nullptr) row = __ldg(p.perm + row);
+    raw[i] = row >= 0 && (p.perm == nullptr || row < p.seq_len)
+                 ? __ldg(reinterpret_cast<const uint4*>(x + row * p.stride_n))
+                 : make_uint4(0, 0, 0, 0);
+  }
   const float pre = job.pre_scale;
 
   // TripPool over the real rows (a prefix of the tile), before pre-scaling,
@@ -277,18 +285,27 @@ extern "C" int veda_quantize(const void* x, int dtype, int64_t stride_n,
   return launch_quant(p, 1, heads, dtype, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int veda_quant_pool(const void* q, const void* k, int dtype,
-                               int64_t stride_n, int64_t stride_h, int n_slots,
-                               int heads, const int32_t* valid_count,
-                               int n_video_tiles, float q_pre_scale,
-                               int8_t* q_i8, float* q_scale, int8_t* k_i8,
-                               float* k_scale, float* feats_q, float* feats_k,
-                               void* stream) {
+namespace {
+
+int quant_pool(const void* q, const void* k, int dtype, int64_t stride_n,
+               int64_t stride_h, int n_slots, int heads,
+               const int32_t* valid_count, int n_video_tiles,
+               float q_pre_scale, int8_t* q_i8, float* q_scale, int8_t* k_i8,
+               float* k_scale, float* feats_q, float* feats_k,
+               const int64_t* perm, int64_t seq_len, void* stream) {
   if (int rc = check_device()) return rc;
-  if (int rc = check_input(q, dtype, stride_n, stride_h, n_slots, heads))
+  // packed inputs have seq_len rows; the check wants a whole number of tiles
+  const int rows = perm == nullptr ? n_slots : kTile;
+  if (int rc = check_input(q, dtype, stride_n, stride_h, rows, heads))
     return rc;
-  if (int rc = check_input(k, dtype, stride_n, stride_h, n_slots, heads))
+  if (int rc = check_input(k, dtype, stride_n, stride_h, rows, heads))
     return rc;
+  if (n_slots <= 0 || n_slots % kTile != 0 || n_slots / kTile > 65535)
+    return fail(VEDA_ERR_INVALID,
+                "slots must be a positive whole number of tiles (at most "
+                "65535)");
+  if (perm != nullptr && seq_len <= 0)
+    return fail(VEDA_ERR_INVALID, "packed input needs seq_len > 0");
   if (q_i8 == nullptr || k_i8 == nullptr || q_scale == nullptr ||
       k_scale == nullptr || !aligned16(q_i8) || !aligned16(k_i8))
     return fail(VEDA_ERR_INVALID, "null or misaligned output");
@@ -307,5 +324,33 @@ extern "C" int veda_quant_pool(const void* q, const void* k, int dtype,
   p.n_tiles = n_tiles;
   p.valid = valid_count;
   p.n_video = feats_q != nullptr ? n_video_tiles : 0;
+  p.perm = perm;
+  p.seq_len = seq_len;
   return launch_quant(p, 2, heads, dtype, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+extern "C" int veda_quant_pool(const void* q, const void* k, int dtype,
+                               int64_t stride_n, int64_t stride_h, int n_slots,
+                               int heads, const int32_t* valid_count,
+                               int n_video_tiles, float q_pre_scale,
+                               int8_t* q_i8, float* q_scale, int8_t* k_i8,
+                               float* k_scale, float* feats_q, float* feats_k,
+                               void* stream) {
+  return quant_pool(q, k, dtype, stride_n, stride_h, n_slots, heads,
+                    valid_count, n_video_tiles, q_pre_scale, q_i8, q_scale,
+                    k_i8, k_scale, feats_q, feats_k, nullptr, 0, stream);
+}
+
+extern "C" int veda_quant_pool_packed(
+    const void* q, const void* k, int dtype, int64_t stride_n,
+    int64_t stride_h, int64_t seq_len, const int64_t* perm, int n_slots,
+    int heads, const int32_t* valid_count, int n_video_tiles,
+    float q_pre_scale, int8_t* q_i8, float* q_scale, int8_t* k_i8,
+    float* k_scale, float* feats_q, float* feats_k, void* stream) {
+  if (perm == nullptr) return fail(VEDA_ERR_INVALID, "null perm");
+  return quant_pool(q, k, dtype, stride_n, stride_h, n_slots, heads,
+                    valid_count, n_video_tiles, q_pre_scale, q_i8, q_scale,
+                    k_i8, k_scale, feats_q, feats_k, perm, seq_len, stream);
 }

@@ -6,10 +6,12 @@ logits, top-k, dense block mask, a host-synchronising index list, quantise
 Q, quantise K, cast V, attend, scatter. This fast path does the same call
 in five kernels with no host synchronisation:
 
-    [gather]  ->  quant_pool (Q, K int8 + TripPool features, one read)
-              ->  tile_logits (predictor; skipped when scores are given)
-              ->  select (top-k straight into ascending index lists)
-              ->  sparse_attention (tcgen05)  ->  [scatter]
+    [gather V] -> quant_pool (Q, K int8 + TripPool features, one read; packed
+                  rows are read through the tile permutation)
+               -> tile_logits (predictor; skipped when scores are given)
+               -> select (top-k straight into ascending index lists)
+               -> sparse_attention (tcgen05; a packed output is written
+                  through the permutation)
 
 `full=True` is a full-attention layer or step (full_attention_layers /
 full_attention_steps, 0% sparsity): the same attention kernel over every
@@ -89,13 +91,17 @@ class VedaAttention:
             tiled = q.shape[0] == layout.num_slots and (
                 layout.identity or q.shape[0] != layout.seq_len)
         tiled_in = tiled
-        head_ids = None
+        perm = None
         if tiled_in:
             q_t, k_t, v_t = q, k, v
         else:
-            head_ids = torch.arange(heads, device=q.device)
-            q_t, k_t, v_t = (ops.gather_tiles(t, layout.perm, head_ids)
-                             for t in (q, k, v))
+            # Packed rows: the quantisation reads Q and K through the
+            # permutation and the attention epilogue writes the output
+            # through it, so only V is gathered into tile order.
+            perm = layout.perm
+            q_t, k_t = q, k
+            v_t = ops.gather_tiles(v, perm,
+                                   torch.arange(heads, device=q.device))
         dim = q.shape[-1]
         scale = dim ** -0.5 if self.softmax_scale is None \
             else self.softmax_scale
@@ -106,7 +112,8 @@ class VedaAttention:
                                layout.n_video_tiles, scale * kernels.LOG2E,
                                pool=need_pool,
                                out=self._buffers.setdefault(
-                                   (tuple(q_t.shape), q_t.device), {}))
+                                   (tuple(q_t.shape), q_t.device), {}),
+                               perm=perm)
         if full:
             index, count = self._dense_lists(layout, heads)
         else:
@@ -119,11 +126,10 @@ class VedaAttention:
                 quant['q_i8'], quant['q_scale'], quant['k_i8'],
                 quant['k_scale'], v_t, index, count, layout.valid_count,
                 out=out)
-        o_t = ops.sparse_attention(quant['q_i8'], quant['q_scale'],
-                                   quant['k_i8'], quant['k_scale'], v_t,
-                                   index, count, layout.valid_count)
         if out is None:
             out = torch.zeros(q.shape[0], heads, dim, dtype=v.dtype,
                               device=q.device)
-        ops.scatter_tiles_(out, o_t, layout.perm, head_ids)
-        return out
+        return ops.sparse_attention(quant['q_i8'], quant['q_scale'],
+                                    quant['k_i8'], quant['k_scale'], v_t,
+                                    index, count, layout.valid_count,
+                                    out=out, perm=perm)

@@ -112,19 +112,27 @@ def quantize(x: torch.Tensor, block: int, pre_scale: float = 1.0):
 
 def quant_pool(q: torch.Tensor, k: torch.Tensor, valid_count: torch.Tensor,
                n_video_tiles: int, q_pre_scale: float, pool: bool = True,
-               out: dict | None = None) -> dict:
+               out: dict | None = None,
+               perm: torch.Tensor | None = None) -> dict:
     """Fused INT8 quantisation of Q (per 128 rows) and K (per 64 rows) and,
     if `pool`, the [mean | max | min] features of the video tiles.
 
-    Returns dict(q_i8, q_scale, k_i8, k_scale, feats_q, feats_k); buffers in
-    `out` with those names are reused.
+    perm: packed input. q and k are then [S, H, 128] in sequence order and
+    tile slot i reads row perm[i] (< 0: padding, zeros): the gather into
+    tile order happens in the same read.
+
+    Returns dict(q_i8, q_scale, k_i8, k_scale, feats_q, feats_k) in tile
+    order; buffers in `out` with those names are reused.
     """
     _check_rows(q, 'q')
     _check_rows(k, 'k')
     if q.shape != k.shape or q.stride() != k.stride() or q.dtype != k.dtype:
         raise ValueError('q and k must share shape, strides and dtype')
     device = require_device(q, k, valid_count)
-    n, heads, _ = q.shape
+    seq_len, heads, _ = q.shape
+    if perm is not None:
+        perm = perm.to(device=device, dtype=torch.int64).contiguous()
+    n = seq_len if perm is None else perm.numel()
     n_tiles = n // TILE
     out = {} if out is None else out
 
@@ -146,11 +154,16 @@ def quant_pool(q: torch.Tensor, k: torch.Tensor, valid_count: torch.Tensor,
         feats_k = buf('feats_k', (heads, n_video_tiles, 3 * HEAD_DIM),
                       torch.float32)
     valid = valid_count.to(torch.int32)
-    _call(device, 'veda_quant_pool', _ptr(q), _ptr(k), _DTYPES[q.dtype],
-              q.stride(0), q.stride(1), n, heads, _ptr(valid), n_video_tiles,
-              ctypes.c_float(q_pre_scale), _ptr(q_i8), _ptr(q_scale),
-              _ptr(k_i8), _ptr(k_scale), _ptr(feats_q), _ptr(feats_k),
-              _stream(device))
+    tail = (_ptr(valid), n_video_tiles, ctypes.c_float(q_pre_scale),
+            _ptr(q_i8), _ptr(q_scale), _ptr(k_i8), _ptr(k_scale),
+            _ptr(feats_q), _ptr(feats_k), _stream(device))
+    if perm is None:
+        _call(device, 'veda_quant_pool', _ptr(q), _ptr(k), _DTYPES[q.dtype],
+              q.stride(0), q.stride(1), n, heads, *tail)
+    else:
+        _call(device, 'veda_quant_pool_packed', _ptr(q), _ptr(k),
+              _DTYPES[q.dtype], q.stride(0), q.stride(1), seq_len, _ptr(perm),
+              n, heads, *tail)
     out['feats_q'], out['feats_k'] = feats_q, feats_k
     return out
 
@@ -221,23 +234,34 @@ def mask_to_index(mask: torch.Tensor, kv_ok: torch.Tensor, width: int):
 
 def sparse_attention(q_i8, q_scale, k_i8, k_scale, v, index, count,
                      valid_count, out: torch.Tensor | None = None,
-                     out_multicast: int = 0):
+                     out_multicast: int = 0,
+                     perm: torch.Tensor | None = None):
     """INT8 block-sparse attention. v [N, H, 128] 16-bit; returns out
     [N, H, 128] of v's dtype (or writes `out`, any row / head strides).
 
     out_multicast: the NVSwitch multicast address of `out`'s first element
     (head sharding): rows are stored through it to every GPU bound to the
     multicast object, instead of to `out` alone.
+    perm: packed output. `out` ([S, H, 128], required) receives row `slot`
+    of the result at row perm[slot]; padding slots (perm < 0) are dropped:
+    the scatter back to sequence order happens in the kernel's epilogue.
     """
     _check_rows(v, 'v')
     device = require_device(q_i8, k_i8, v, index, count, valid_count)
     n, heads, _ = v.shape
     n_tiles = n // TILE
+    if perm is not None and (out is None or out_multicast):
+        raise ValueError('a packed output needs `out` and no multicast')
     if out is None:
         out = torch.empty(n, heads, HEAD_DIM, dtype=v.dtype, device=device)
     _check_rows(out, 'out')
     if out.dtype != v.dtype:
         raise ValueError('out must have v\'s dtype')
+    if perm is not None:
+        perm = perm.to(device=device, dtype=torch.int64).contiguous()
+        if perm.numel() != n or out.shape[1] != heads:
+            raise ValueError('perm must have a slot per row of v, and out '
+                             'v\'s heads')
     index = index.to(torch.int32).contiguous()
     count = count.to(torch.int32).contiguous()
     valid = valid_count.to(torch.int32).contiguous()
@@ -250,6 +274,9 @@ def sparse_attention(q_i8, q_scale, k_i8, k_scale, v, index, count,
     if out_multicast:
         _call(device, 'veda_sparse_attention_multicast', *head,
               ctypes.c_void_p(out_multicast), *tail)
+    elif perm is not None:
+        _call(device, 'veda_sparse_attention_packed', *head, out.stride(0),
+              out.stride(1), _ptr(perm), out.shape[0], *tail[2:])
     else:
         _call(device, 'veda_sparse_attention', *head, *tail)
     return out
