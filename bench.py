@@ -33,9 +33,7 @@ import argparse
 import json
 import math
 import os
-import re
 import statistics
-import subprocess
 import sys
 import time
 
@@ -112,71 +110,95 @@ def measure_int8_peak(device) -> float:
     return 2 * n ** 3 / (best * 1e-3) / 1e12
 
 
-def profile_traffic() -> float | None:
-    """DRAM bytes per attention launch from the committed ncu summary."""
-    path = os.path.join(HERE, 'profiles', 'sparse_attention_cfg1.md')
-    if not os.path.exists(path):
-        return None
-    with open(path) as f:
-        m = re.search(r'traffic_bytes_per_launch:\s*([0-9.eE+]+)', f.read())
-    return float(m.group(1)) if m else None
+# DRAM bytes (read + write) of one attention launch at cfg1, from the ncu
+# capture of the kernel this file runs: `dram__bytes_read.sum +
+# dram__bytes_write.sum` of sparse_attention_kernel<bf16>. The capture
+# needs a profiler, so it cannot be taken inside a timed run; the figure is
+# refreshed whenever the kernel changes and `TRAFFIC_SOURCE` names the
+# capture it came from.
+TRAFFIC_BYTES = None
+TRAFFIC_SOURCE = None
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 50 ms."""
+    """SM clocks and clock-event (throttle) reasons, polled through NVML
+    every millisecond on a host thread while the timed region runs, so a
+    timed region of a few tens of milliseconds still gets samples. Reads
+    only; nothing is set."""
 
-    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,'
-              'clocks_event_reasons.hw_slowdown,'
-              'clocks_event_reasons.hw_thermal_slowdown,'
-              'clocks_event_reasons.sw_thermal_slowdown,'
-              'clocks_event_reasons.sw_power_cap')
+    # NVML clock-event reason bits (nvml.h nvmlClocksEventReason*)
+    REASONS = {'sw_power_cap': 0x4, 'hw_slowdown': 0x8,
+               'sw_thermal_slowdown': 0x20, 'hw_thermal_slowdown': 0x40}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
+        self.samples = []   # (sm_mhz, reasons bitmask)
+        self.max_mhz = None
+        self.error = None
+
+    def _poll(self):
+        import pynvml
+        while not self._stop.is_set():
+            try:
+                sm = pynvml.nvmlDeviceGetClockInfo(self._handle,
+                                                   pynvml.NVML_CLOCK_SM)
+                why = pynvml.nvmlDeviceGetCurrentClocksEventReasons(
+                    self._handle)
+                self.samples.append((float(sm), int(why)))
+            except Exception as error:  # noqa: BLE001 - reported
+                self.error = str(error)
+                return
+            time.sleep(0.001)
 
     def __enter__(self):
+        import threading
+        self._stop = threading.Event()
+        self._thread = None
         try:
-            self.proc = subprocess.Popen(
-                ['nvidia-smi', f'--id={self.index}',
-                 f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
-                 '-lms', '50'], stdout=subprocess.PIPE,
-                stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = torch.cuda.get_device_properties(self.index).uuid
+            self._handle = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                got = pynvml.nvmlDeviceGetUUID(h)
+                got = got.decode() if isinstance(got, bytes) else got
+                if str(uuid) in got:
+                    self._handle = h
+            if self._handle is None:
+                self._handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(
+                self._handle, pynvml.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._poll, daemon=True)
+        except Exception as error:  # noqa: BLE001 - no NVML: no samples
+            self.error = str(error)
         return self
 
+    def start(self):
+        """Begins polling (call right before the timed region)."""
+        if self._thread is not None:
+            self._thread.start()
+
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        self._stop.set()
+        if self._thread is not None and self._thread.is_alive():
+            self._thread.join(timeout=5)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown',
-                 'sw_power_cap']
-        for line in getattr(self, 'lines', []):
-            parts = [p.strip() for p in line.split(',')]
-            if len(parts) < 8:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[4:8]):
-                if flag.lower() == 'active':
+        sm = [s for s, _ in self.samples]
+        reasons = set()
+        for _, bits in self.samples:
+            for name, bit in self.REASONS.items():
+                if bits & bit:
                     reasons.add(name)
-        loaded = [s for s in sm if mx and s > 0.5 * mx] or sm
-        return {'sm_mhz': statistics.median(loaded) if loaded else None,
-                'sm_max_mhz': mx, 'samples': len(sm),
-                'reasons': sorted(reasons)}
+        loaded = [s for s in sm if self.max_mhz and s > 0.5 * self.max_mhz] \
+            or sm
+        out = {'sm_mhz': statistics.median(loaded) if loaded else None,
+               'sm_max_mhz': self.max_mhz, 'samples': len(sm),
+               'reasons': sorted(reasons), 'source': 'NVML, 1 ms polling'}
+        if self.error:
+            out['error'] = self.error[:200]
+        return out
 
 
 # ------------------------------------------------------------ workload
@@ -206,9 +228,11 @@ class Call:
     """One Veda attention call on this rank's heads (the timed step)."""
 
     def __init__(self, n_local: int, device, group=None, world=1):
-        from veda_b200 import kernels, selection, sharding, tiling
+        from veda_b200 import engine, kernels, selection, sharding, tiling
         self.kernels = kernels
         self.layout = tiling.identity_layout(REAL, device)
+        # the public API a user calls: the engine's layer
+        self.engine = engine.VedaAttention(selection.Budget(tiles=KEEP))
         self.blocks = selection.column_blocks(
             self.layout, selection.Budget(tiles=KEEP),
             selection.Budget(ratio=1.0))
@@ -277,6 +301,19 @@ class Call:
         rec(4)
         return count
 
+    def via_engine(self, s: dict):
+        """The same call through the public API, `VedaAttention.layer`
+        (select, quantise, attend: three of this build's kernels), then the
+        same exchange."""
+        self.engine.layer(s['q'], s['k'], s['v'], self.layout,
+                          scores=s['scores'], out=self.out,
+                          out_multicast=self.out_mc)
+        if self.mc is not None:
+            self.mc.complete()
+        elif self.gathered is not None:
+            torch.distributed.all_gather_into_tensor(self.gathered, self.out,
+                                                     group=self.group)
+
     def check_exchange(self, s: dict) -> bool:
         """The multicast output equals an NCCL all-gather of the plain
         kernel's per-rank outputs, bit for bit (untimed self-check)."""
@@ -295,50 +332,100 @@ class Call:
         return bool(torch.equal(full, want))
 
 
+def _reference_cpu_modules():
+    """(reference, selection, tiling) of the reference's torch core from the
+    unmodified package in baseline/_ref, or None when it is absent."""
+    ref = os.path.join(HERE, 'baseline', '_ref')
+    if not os.path.isdir(os.path.join(ref, 'veda_comfy')):
+        return None
+    if ref not in sys.path:
+        sys.path.append(ref)
+    try:
+        from veda_comfy.core import reference, selection, tiling
+    except Exception:  # noqa: BLE001 - fall back to the port
+        return None
+    return reference, selection, tiling
+
+
+def _cpu_head(seed: int = 2024):
+    """One head of the workload on the host: q, k, v [SEQ, 1, 128] (bf16
+    values held in fp32, rows past REAL zero) and scores [1, 256, 256]."""
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn(SEQ, 1, DIM, generator=g) for _ in range(3))
+    k = k + torch.randn(DIM, generator=g) * 2.0
+    q, k, v = (t.to(torch.bfloat16).float() for t in (q, k, v))
+    for t in (q, k, v):
+        t[REAL:] = 0
+    return q, k, v, torch.rand(1, N_TILES, N_TILES, generator=g)
+
+
 def cpu_reference(seconds_hint: float = 15.0) -> dict:
-    """The reference's CPU path for one head of the workload (selection +
-    fp32 masked attention, oracle/ numpy restatement), timed on the host."""
+    """The reference's CPU path for one head of the workload, timed on the
+    host with every core: its own torch code from baseline/_ref
+    (core/selection.py select, block_mask and tile_index_list, then
+    core/reference.py block_sparse_attention, fp32 masked attention over the
+    whole head), or, when that package is absent, the oracle's numpy port of
+    the same functions on a bounded number of query rows."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    q, k, v, scores = _cpu_head()
+    mods = _reference_cpu_modules()
+    if mods is not None:
+        rref, rsel, rtil = mods
+        layout = reference_layout(rtil, None, SEQ, REAL, 'cpu')
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            blocks = rsel.column_blocks(layout, rsel.Budget(tiles=KEEP),
+                                        rsel.Budget(ratio=1.0))
+            index, keep = rsel.select(scores, layout, blocks)
+            mask = rsel.block_mask(index, keep, layout)
+            _, count = rsel.tile_index_list(mask)
+            rref.block_sparse_attention(q, k, v, mask, layout)
+        elapsed = time.perf_counter() - t0
+        pairs = int(count.sum())
+        return {'value': pairs * OPS_PER_PAIR / elapsed / 1e12,
+                'unit': 'TFLOPS', 'cores': torch.get_num_threads(),
+                'kind': 'reference', 'seconds': elapsed,
+                'sample': f'1 of 24 heads, all {SEQ} query rows: the '
+                          'reference\'s own torch CPU code from '
+                          'baseline/_ref (core/selection.py select + '
+                          'block_mask + tile_index_list, core/reference.py '
+                          'block_sparse_attention in fp32), '
+                          f'{torch.get_num_threads()} host threads'}
     from oracle import attention as oatt
     from oracle import selection as osel
     from oracle import tiling as otil
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(2024)
-    q, k, v = (torch.randn(SEQ, DIM, generator=g) for _ in range(3))
-    k = k + torch.randn(DIM, generator=g) * 2.0
-    q, k, v = (t.to(torch.bfloat16).float().numpy() for t in (q, k, v))
-    q[REAL:] = k[REAL:] = v[REAL:] = 0
-    scores = torch.rand(1, N_TILES, N_TILES, generator=g).numpy()
+    qn, kn, vn = (t[:, 0].numpy() for t in (q, k, v))
     layout = otil.identity_layout(REAL)
     t0 = time.perf_counter()
     blocks = osel.column_blocks(layout, osel.Budget(tiles=KEEP),
                                 osel.Budget(ratio=1.0))
-    index, count = osel.index_lists(scores, layout, blocks)
+    index, count = osel.index_lists(scores.numpy(), layout, blocks)
     mask = oatt.mask_from_lists(index, count, layout.n_tiles)[0]
     rows_done, pairs = 0, 0
     chunk = 2048
     while rows_done < SEQ:
         rows = np.arange(rows_done, rows_done + chunk)
-        oatt.block_sparse_head(q, k, v, mask, layout.slot_valid, rows=rows)
+        oatt.block_sparse_head(qn, kn, vn, mask, layout.slot_valid, rows=rows)
         pairs += int(count[0, rows_done // 128:(rows_done + chunk) // 128]
                      .sum())
         rows_done += chunk
         if time.perf_counter() - t0 > seconds_hint:
             break
     elapsed = time.perf_counter() - t0
-    tflops = pairs * OPS_PER_PAIR / elapsed / 1e12
-    return {'value': tflops, 'unit': 'TFLOPS', 'cores': threads,
-            'kind': 'port', 'seconds': elapsed,
+    return {'value': pairs * OPS_PER_PAIR / elapsed / 1e12, 'unit': 'TFLOPS',
+            'cores': threads, 'kind': 'port', 'seconds': elapsed,
             'sample': f'1 of 24 heads, {rows_done} of {SEQ} query rows: '
-                      'reference selection + fp32 masked attention '
-                      '(oracle numpy port of core/selection.py and '
-                      'core/reference.py), '
-                      f'{threads} host threads'}
+                      'oracle numpy port of core/selection.py and '
+                      'core/reference.py (the reference package is not in '
+                      f'baseline/_ref), {threads} host threads'}
 
 
 # ---------------------------------------------------------------- main
 
 def run_reference(args, rank: int, json_out):
+    """The reference arm of the driver: the reference's own CPU path of the
+    workload (see `cpu_reference`), one head per step, on rank 0 only."""
     if rank != 0:
         return
     samples = []
@@ -355,7 +442,8 @@ def run_reference(args, rank: int, json_out):
             'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
             'config': {'workload': WORKLOAD, 'sample': samples[0]['sample']},
             'cpu_baseline': {'value': value, 'unit': 'TFLOPS',
-                             'cores': samples[0]['cores'], 'kind': 'port',
+                             'cores': samples[0]['cores'],
+                             'kind': samples[0]['kind'],
                              'sample': samples[0]['sample']},
             'e2e': {'value': value, 'unit': 'TFLOPS',
                     'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
@@ -676,12 +764,12 @@ def main():
               for _ in range(args.steps)]
     start, end = torch.cuda.Event(True), torch.cuda.Event(True)
     with ClockSampler(local) as clocks:
-        # warm-up inside the sampler, so the clocks are sampled under load
         for i in range(args.warmup):
             call(sets[i % n_sets])
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
+        clocks.start()
         start.record()
         for i in range(args.steps):
             call(sets[i % n_sets], events[i])
@@ -694,7 +782,8 @@ def main():
                        for e in events])             # steps x 4
     work_pairs = sum(pairs[i % n_sets] for i in range(args.steps))
 
-    # ---- e2e: host buffers in, result out, inside the timed region.
+    # ---- e2e: host buffers in, result out, inside the timed region,
+    # through the engine's public `layer` call.
     # Consecutive calls run the way a serving loop runs them: the inputs of
     # call i + 1 copy in on one stream while call i computes, and call i's
     # output copies out on another while call i + 1's inputs are still
@@ -729,7 +818,7 @@ def main():
             comp.wait_event(arrived[i])
             if i >= 1:  # call i - 1's output has been read out
                 comp.wait_event(read[i - 1])
-            call(buf)
+            call.via_engine(buf)
             done[i].record(comp)
             with torch.cuda.stream(d2h_stream):
                 d2h_stream.wait_event(done[i])
@@ -773,7 +862,6 @@ def main():
         # the attention kernel on rank 0: its own pairs over its own time
         attn_ops = work_pairs / args.steps * OPS_PER_PAIR
         achieved = attn_ops / (attn_ms * 1e-3) / 1e12
-        traffic = profile_traffic()
         line = {
             'metric': METRIC, 'value': value, 'unit': 'TFLOPS',
             'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
@@ -797,7 +885,8 @@ def main():
                 'bound': 'tensor', 'kernel': 'sparse_attention_kernel',
                 'achieved': achieved, 'peak': mixed_peak,
                 'unit': 'TFLOP/s', 'frac': achieved / mixed_peak,
-                'traffic': traffic,
+                'traffic': TRAFFIC_BYTES,
+                'traffic_source': TRAFFIC_SOURCE,
                 'peak_note': (f'harmonic mix of measured INT8 '
                               f'{int8_tops:.0f} TOPS (torch._int_mm 8192^3, '
                               f'best of 10, this run) and bf16 {bf16} '
@@ -807,6 +896,7 @@ def main():
                     1e12, 'unit': 'TFLOPS', 'ms_per_step': e2e_ms,
                     'h2d_bytes_per_step': int(h2d_all),
                     'd2h_bytes_per_step': int(d2h_all),
+                    'api': 'veda_b200.engine.VedaAttention.layer',
                     'overlap': 'copies of neighbouring calls overlap a '
                                'call (H2D and D2H streams); each call '
                                'moves all of its own bytes'},

@@ -108,12 +108,15 @@ int veda_tile_logits(const float* feats_q, const float* feats_k,
  * features) is a fixed 8 MiB device array inside this library, one per
  * device, instead of a caller workspace. This entry point has no
  * counterpart in the reference, whose predictor allocates through torch.
- *   Limit: (n_q + n_k) * heads <= VEDA_STATIC_LOGITS_ROWS; larger calls
- *   return VEDA_ERR_INVALID before any work.
+ *   Limit: n_q, n_k and (n_q + n_k) * heads each <= VEDA_STATIC_LOGITS_ROWS;
+ *   larger calls return VEDA_ERR_INVALID before any device work (the
+ *   sizes are checked before the device).
  *   Calls that overlap in time on one device (other streams or threads)
  *   share the array and race: serialise them.
- *   The first call on each device looks up the array's address (with that
- *   device current); make it before any stream capture.
+ *   Each call looks up the array's address in the current device's context
+ *   (so a device reset, which reloads the module, is followed correctly).
+ *   The first call on a device loads the module if it is not yet loaded:
+ *   make it before any stream capture.
  * Arguments and results are those of veda_tile_logits.
  */
 int veda_tile_logits_static(const float* feats_q, const float* feats_k,
@@ -215,6 +218,10 @@ int veda_sparse_attention_multicast(
  * padding, zeros), so the gather of core/tiling.py:227-242 (gather_tiles)
  * happens in the same read. Outputs as veda_quant_pool, same bits as
  * veda_gather_tiles followed by veda_quant_pool. perm has n_slots entries.
+ * The caller guarantees that q and k hold seq_len rows at the given
+ * strides and that every perm entry is below seq_len: rows at or past
+ * seq_len are treated as padding, but seq_len itself is not checked
+ * against the tensors (raw pointers carry no extent).
  */
 int veda_quant_pool_packed(
     const void* q, const void* k, int dtype, int64_t stride_n,
@@ -229,6 +236,8 @@ int veda_quant_pool_packed(
  * strides), padding slots (perm < 0) are dropped, so the scatter of
  * core/tiling.py:245-252 (scatter_tiles_) happens in the kernel's epilogue.
  * Same bits as veda_sparse_attention followed by veda_scatter_tiles.
+ * The caller guarantees that `out` holds seq_len rows at the given strides;
+ * slots whose perm entry is at or past seq_len are dropped like padding.
  */
 int veda_sparse_attention_packed(
     const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,

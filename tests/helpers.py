@@ -76,8 +76,16 @@ MAX_ABS = 2e-2
 
 
 def within_int8_tolerance(m: dict) -> bool:
-    """The attention tolerance: cos >= 0.9995 and max |diff| <= 2e-2 at
-    unit output scale (2e-2 x max |want| when outputs exceed 1, since the
-    reference's own fp16 PV accumulation errs in proportion to them)."""
+    """The attention tolerance of every benchmark configuration: cos >=
+    0.9995 and max |diff| <= 2e-2, flat (not scaled by the output)."""
+    return m['cos'] >= COS_MIN and m['max_abs'] <= MAX_ABS
+
+
+def within_selftest_tolerance(m: dict) -> bool:
+    """The same bar scaled by the output's magnitude, for the reference's
+    self-test problem only: its inputs are 1.5 N(0,1), and there the
+    reference's own Triton kernel and its own INT8 model already differ by
+    0.029, because the kernel sums each 64-key block of P V in fp16, an
+    error that grows with the output."""
     return m['cos'] >= COS_MIN and m['max_abs'] <= MAX_ABS * max(
         1.0, m['absmax'])

@@ -104,3 +104,19 @@ def test_library_is_sm100a_only():
     """The build flags name one target, sm_100a, and no PTX fallback."""
     from veda_b200 import build
     assert build.ARCH == ['-gencode', 'arch=compute_100a,code=sm_100a']
+
+
+def test_static_logits_rejects_oversize_sizes_before_any_device_work():
+    """veda_tile_logits_static checks its sizes before it looks at a device,
+    with 64-bit arithmetic: n_q = n_k = 2^30 (whose int sum overflows) is
+    refused with VEDA_ERR_INVALID here, on a machine with no GPU at all.
+    The pointers are never dereferenced."""
+    from veda_b200 import _lib
+    lib = _lib.load()
+    fake = ctypes.c_void_p(256)
+    for heads, n_q, n_k in [(1, 2 ** 30, 2 ** 30), (1, 20000, 1),
+                            (24, 256, 512), (65535, 1, 1)]:
+        rc = lib.veda_tile_logits_static(fake, fake, fake, fake, _lib.BF16,
+                                         heads, n_q, n_k, fake, None)
+        assert rc == _lib.ERR_INVALID, (heads, n_q, n_k, rc)
+        assert b'static scratch limit' in lib.veda_last_error()

@@ -227,8 +227,9 @@ def test_attention_zero_count_rows_are_zero(cuda_device):
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
 def test_attention_matches_reference_fixture(cuda_device, name, dtype):
     """The north-star tolerance against the reference's own INT8 kernel
-    (run on the same inputs under Triton's interpreter), and the reference
-    backend's 5%-of-absmax check against fp32 masked attention."""
+    (run on the same inputs under Triton's interpreter; output-scaled for
+    the self-test problem only), and the reference backend's 5%-of-absmax
+    check against fp32 masked attention."""
     from veda_b200 import selection as vs
     case = problems.CASES[name]
     info = helpers.meta()['attention'][name]
@@ -246,7 +247,9 @@ def test_attention_matches_reference_fixture(cuda_device, name, dtype):
     ref_int8 = gold[f'{name}.int8_out'].astype(np.float32)[real]
     fp32 = gold[f'{name}.fp32_out'][real]
     m = helpers.compare(got, ref_int8)
-    assert helpers.within_int8_tolerance(m), m
+    within = helpers.within_selftest_tolerance if name == 'selftest' else \
+        helpers.within_int8_tolerance
+    assert within(m), m
     m32 = helpers.compare(got, fp32)
     assert m32['max_rel'] < 0.05, m32
 

@@ -12,7 +12,7 @@ size the checks are properties that hold at any size:
     path bit for bit.
 Cases: cfg1 (config 1), the full-attention layer of config 2 at cfg1 size,
 config 3 at 131,072 tokens, config 4 (generated + global reference tiles),
-and the reference's own self-test through `Backend`.
+and the self-test problem through `Backend.attend`.
 """
 
 import numpy as np
@@ -200,16 +200,23 @@ def test_engine_predictor_path_selects_on_its_own_logits(cuda_device):
     assert torch.equal(out, direct)
 
 
-def test_backend_passes_the_reference_self_test(cuda_device):
-    """The reference's node-execution validation (backends/base.py:123-155)
-    and `attend` with a dense block mask."""
+def test_backend_attend_with_a_mask_equals_the_list_path(cuda_device):
+    """`Backend.attend` with the reference's dense block mask (the self-test
+    problem: mixed spans, partial tiles, global rows) gives the same bits as
+    the kernel package on the lists the mask stands for; the reference's
+    own self-test of this backend is in test_reference_boundary.py."""
     from veda_b200 import backend, kernels, selection
+    case = problems.CASES['selftest']
+    q, k, v, scores, olayout = problems.make_problem(case)
+    layout = helpers.device_layout(case, cuda_device)
+    index, count = selection.select_index(
+        torch.from_numpy(scores).to(cuda_device), layout,
+        helpers.product_blocks(case, layout))
+    mask = backend.mask_from_lists(index, count, layout.n_tiles)
     b = backend.create(cuda_device)
     for dtype in b.dtypes:
-        backend.self_test(b, cuda_device, dtype)
-    q, k, v, mask, layout = backend.selftest_problem(cuda_device,
-                                                     torch.bfloat16, seed=3)
-    out = b.attend(q, k, v, mask, layout)
-    index, count = selection.tile_index_list(mask, layout.kv_ok)
-    assert torch.equal(out, kernels.attend(q, k, v, index, count,
-                                           layout.valid_count))
+        dq, dk, dv = (t.to(dtype).to(cuda_device) for t in (q, k, v))
+        out = b.attend(dq, dk, dv, mask, layout)
+        lists = selection.tile_index_list(mask, layout.kv_ok)
+        assert torch.equal(out, kernels.attend(dq, dk, dv, *lists,
+                                               layout.valid_count))

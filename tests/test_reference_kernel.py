@@ -6,8 +6,17 @@ inputs and index lists.
 
 The reference rounds P and V to fp16 and sums P V per 64-key block in
 fp16; this build keeps P in the input's 16-bit type and accumulates in
-fp32, so the bar is the attention tolerance (cos >= 0.9995, max |diff|
-<= 2e-2 at unit scale), not bit equality.
+fp32, so the bar is the attention tolerance, not bit equality: cos >=
+0.9995 and max |diff| <= 2e-2 over the WHOLE output (every head, every
+real row), at every benchmark configuration and length:
+  cfg1   24 heads, 32,760 tokens, 26 of 256 tiles
+  cfg2   one sparse and one full-attention layer of the 48-layer step
+  cfg3   24 heads at 16,384 / 32,768 / 65,536 / 131,072 tokens, 90% sparse
+  cfg4   24,576 generated + 8,192 reference tokens (global tiles)
+Inputs are drawn on the GPU from fixed seeds (both kernels read the same
+tensors, so nothing needs to match a CPU draw); the lists come from this
+build's select kernel, which the selection tests pin bit for bit to the
+reference's torch selection.
 """
 
 import os
@@ -37,24 +46,89 @@ def _reference():
     return sparse_int8
 
 
+def _compare_full(got, want, real):
+    """Flat bar over every real row of every head, computed on the GPU."""
+    g = got[real].float()
+    w = want[real].float()
+    cos = float((g * w).sum() / (g.norm() * w.norm()))
+    err = float((g - w).abs().max())
+    return {'cos': cos, 'max_abs': err, 'absmax': float(w.abs().max())}
+
+
+def _draw(seq, heads, device, seed, k_offset=0.0, real=None):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    q, k, v = (torch.randn(seq, heads, 128, generator=g, device=device)
+               for _ in range(3))
+    if k_offset:
+        k = k + torch.randn(heads, 128, generator=g, device=device) * k_offset
+    if real is not None:
+        for t in (q, k, v):
+            t[real:] = 0
+    return q, k, v, g
+
+
+# name: (seq_len, real, k_offset, budget, spans, full)
+CONFIGS = {
+    'cfg1': (32768, 32760, 2.0, ('tiles', 26), None, False),
+    'cfg2_full_layer': (32768, 32760, 2.0, None, None, True),
+    'cfg3_16k': (16384, None, 0.0, ('sparsity', 90), None, False),
+    'cfg3_32k': (32768, None, 0.0, ('sparsity', 90), None, False),
+    'cfg3_64k': (65536, None, 0.0, ('sparsity', 90), None, False),
+    'cfg3_131k': (131072, None, 0.0, ('sparsity', 90), None, False),
+    'cfg4': (32768, None, 0.0, ('tiles', 32),
+             ((8192, (1, 1, 24576), (1, 1, 128)),), False),
+}
+
+
+@pytest.mark.parametrize('name', list(CONFIGS))
+def test_full_output_matches_reference_triton_kernel(cuda_device, name):
+    ref = _reference()
+    from veda_b200 import kernels, selection, tiling
+    seq, real, k_offset, budget, spans, full = CONFIGS[name]
+    heads = 24
+    q, k, v, g = _draw(seq, heads, cuda_device, 4000 + seq // 1024 +
+                       (7 if spans else 0), k_offset, real)
+    if spans is None:
+        layout = tiling.identity_layout(seq if real is None else real,
+                                        cuda_device)
+    else:
+        layout = tiling.build_tile_layout(
+            [tiling.TiledSpan(s, tuple(d), tiling.TileShape(*t))
+             for s, d, t in spans], seq, cuda_device)
+    if full:
+        index, count = selection.dense_index(layout, heads)
+    else:
+        gen = selection.Budget(tiles=budget[1]) if budget[0] == 'tiles' \
+            else selection.Budget.sparsity(budget[1])
+        blocks = selection.column_blocks(layout, gen,
+                                         selection.Budget(ratio=1.0))
+        n = layout.n_video_tiles
+        scores = torch.rand(heads, n, n, generator=g, device=cuda_device)
+        index, count = selection.select_index(scores, layout, blocks)
+    q, k, v = (t.to(torch.bfloat16).contiguous() for t in (q, k, v))
+    want = ref.attend(q, k, v, index, count, layout.valid_count)
+    got = kernels.attend(q, k, v, index, count, layout.valid_count)
+    m = _compare_full(got, want, layout.slot_valid.bool())
+    assert m['cos'] >= helpers.COS_MIN and m['max_abs'] <= helpers.MAX_ABS, m
+
+
 @pytest.mark.parametrize('name', ['gpu_problem', 'cfg1'])
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
 def test_attention_matches_reference_triton_kernel(cuda_device, name, dtype):
+    """The fixture problems (CPU-drawn inputs), in both 16-bit types."""
     ref = _reference()
     from veda_b200 import kernels
     from veda_b200 import selection as vs
     case = problems.CASES[name]
     q, k, v, scores, olayout = problems.make_problem(case)
-    heads = min(case.heads, 4)  # four heads keep the cfg1 case quick
-    q, k, v = (t[:, :heads].to(dtype).contiguous().to(cuda_device)
-               for t in (q, k, v))
+    q, k, v = (t.to(dtype).contiguous().to(cuda_device) for t in (q, k, v))
     layout = helpers.device_layout(case, cuda_device)
     index, count = vs.select_index(
-        torch.from_numpy(scores[:heads]).to(cuda_device), layout,
+        torch.from_numpy(scores).to(cuda_device), layout,
         helpers.product_blocks(case, layout))
     want = ref.attend(q, k, v, index, count, layout.valid_count)
     got = kernels.attend(q, k, v, index, count, layout.valid_count)
     real = torch.from_numpy(olayout.slot_valid.astype(bool)).to(cuda_device)
-    m = helpers.compare(got[real].float().cpu().numpy(),
-                        want[real].float().cpu().numpy())
-    assert helpers.within_int8_tolerance(m), m
+    m = _compare_full(got, want, real)
+    assert m['cos'] >= helpers.COS_MIN and m['max_abs'] <= helpers.MAX_ABS, m

@@ -57,11 +57,17 @@ def test_static_scratch_logits_equal_the_workspace_entry_point(cuda_device):
         got = torch.full_like(want, float('nan'))
         assert _with_workspace(lib, stream, *inputs, want) == 0, \
             lib.veda_last_error()
+        # a first call loads the module (and its static array) if needed
+        assert _static(lib, stream, *inputs, got) == 0, lib.veda_last_error()
+        got.fill_(float('nan'))
         torch.cuda.synchronize(cuda_device)
-        before = torch.cuda.memory_allocated(cuda_device)
+        # free device memory as the driver sees it, so an allocation made
+        # by the library itself (not only torch's) would show
+        free_before, _ = torch.cuda.mem_get_info(cuda_device)
         assert _static(lib, stream, *inputs, got) == 0, lib.veda_last_error()
         torch.cuda.synchronize(cuda_device)
-        assert torch.cuda.memory_allocated(cuda_device) == before
+        free_after, _ = torch.cuda.mem_get_info(cuda_device)
+        assert free_after == free_before
         assert torch.equal(got, want)
 
 

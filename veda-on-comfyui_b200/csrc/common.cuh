@@ -86,22 +86,29 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 
 // Waits for the phase of `bar` with the given parity to complete. Gives up
 // when another role of the CTA has aborted (`*abort` set) or after
-// kWaitLimitNs; on a timeout it sets `*abort` and reports `code`.
+// `limit_ns`; on a timeout it sets `*abort` and reports `code`.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort, int32_t* status,
-                                          int32_t code) {
+                                          int32_t code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_test(bar, parity)) return true;
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (global_ns() - start > kWaitLimitNs) {
+    if (global_ns() - start > limit_ns) {
       *abort = 1;
       report(status, code);
       return false;
     }
   }
+}
+
+// Named barrier `id` (1-15) over `threads` threads (a multiple of 32); every
+// warp taking part executes it whole.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // ------------------------------------------------------------------- TMA
@@ -317,6 +324,18 @@ __device__ __forceinline__ void reg_fence32(uint32_t* r) {
       : "memory");
 }
 
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
+      "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]),
+      "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -325,6 +344,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// max(a, b, c) in one instruction (three-operand max.f32, sm_100+).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // ------------------------------------------------ packed fp32 (sm_100+)

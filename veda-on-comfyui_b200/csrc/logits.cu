@@ -4,7 +4,6 @@
 // fp32 on CUDA cores: about 1.2 GFLOP for 24 heads x 256 tiles, far below
 // anything worth a tensor-core pipeline, and fp32 keeps the logits (and so
 // the selection) within rounding of the reference's fp32 bmm.
-#include <mutex>
 
 #include "common.cuh"
 
@@ -106,28 +105,16 @@ __global__ void __launch_bounds__(256)
 static __device__ __align__(256) float g_static_logits_scratch[
     static_cast<int64_t>(VEDA_STATIC_LOGITS_ROWS) * kDim];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_static_mutex;
-float* g_static_scratch[kMaxDevices] = {};
-
-// Address of the scratch on the current device, looked up once per device
-// (with that device current, as cudaGetSymbolAddress requires).
+// Address of the scratch in the current device's context. It is looked up on
+// every call rather than cached: after a device reset the module is loaded
+// again and the array may sit at another address.
 int static_scratch(float** out) {
-  int device = 0;
-  VEDA_CHECK_CUDA(cudaGetDevice(&device));
-  if (device < 0 || device >= kMaxDevices)
-    return fail(VEDA_ERR_UNSUPPORTED, "device %d is past the %d this library "
-                "tracks", device, kMaxDevices);
-  std::lock_guard<std::mutex> lock(g_static_mutex);
-  if (g_static_scratch[device] == nullptr) {
-    void* address = nullptr;
-    const cudaError_t err =
-        cudaGetSymbolAddress(&address, g_static_logits_scratch);
-    if (err != cudaSuccess)
-      return cuda_fail(err, "cudaGetSymbolAddress(static logits scratch)");
-    g_static_scratch[device] = static_cast<float*>(address);
-  }
-  *out = g_static_scratch[device];
+  void* address = nullptr;
+  const cudaError_t err =
+      cudaGetSymbolAddress(&address, g_static_logits_scratch);
+  if (err != cudaSuccess)
+    return cuda_fail(err, "cudaGetSymbolAddress(static logits scratch)");
+  *out = static_cast<float*>(address);
   return VEDA_OK;
 }
 
@@ -203,16 +190,19 @@ extern "C" int veda_tile_logits_static(const float* feats_q,
                                        const void* proj_q, const void* proj_k,
                                        int proj_dtype, int heads, int n_q,
                                        int n_k, float* logits, void* stream) {
-  if (int rc = check_device()) return rc;
+  // Sizes first, before anything touches a device: a call past the limit
+  // is the caller's error whatever the device.
   if (int rc = check_logits_args(feats_q, feats_k, proj_q, proj_k, heads, n_q,
                                  n_k, logits))
     return rc;
-  const int64_t rows = static_cast<int64_t>(n_q + n_k) * heads;
-  if (rows > VEDA_STATIC_LOGITS_ROWS)
+  const int64_t rows = (static_cast<int64_t>(n_q) + n_k) * heads;
+  if (n_q > VEDA_STATIC_LOGITS_ROWS || n_k > VEDA_STATIC_LOGITS_ROWS ||
+      rows > VEDA_STATIC_LOGITS_ROWS)
     return fail(VEDA_ERR_INVALID,
                 "(n_q + n_k) * heads = %lld rows exceeds the static scratch "
                 "limit of %d rows; use veda_tile_logits with a workspace",
                 static_cast<long long>(rows), VEDA_STATIC_LOGITS_ROWS);
+  if (int rc = check_device()) return rc;
   float* scratch = nullptr;
   if (int rc = static_scratch(&scratch)) return rc;
   return launch_tile_logits(feats_q, feats_k, proj_q, proj_k, proj_dtype,

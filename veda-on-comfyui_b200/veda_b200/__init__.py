@@ -11,7 +11,7 @@ A thin C ABI (include/veda_b200.h, built into libveda_b200.so by
                     tensor cores with TMEM accumulators, TMA tile loads
 
 and, above it, the reference's interfaces for this path: the backend
-contract (`backend.Backend`, `self_test`), the kernel API
+contract (`backend.Backend`, `backend.create`), the kernel API
 (`kernels.attend`), the selection and tiling rules, an engine fast path
 (`engine.VedaAttention`) and head sharding across GPUs (`sharding`).
 Nothing here has a CPU fallback.

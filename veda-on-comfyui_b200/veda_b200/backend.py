@@ -1,18 +1,21 @@
-"""The reference's backend contract (veda_comfy/backends/base.py) and the
-B200 backend that implements it over the sm_100a library.
+"""The backend interface of the reference (veda_comfy/backends/base.py) and
+the B200 backend behind it.
 
-`Backend.attend(q, k, v, block_mask, layout) -> out` has the reference's
-argument meaning (base.py:61-77): q / k / v [N, H', 128] contiguous in tile
-order with zero padding slots, block_mask [H', n_tiles, n_tiles] bool with
-query tiles as rows, `layout` a tile layout (this package's TileLayout or
-the reference's own: only valid_count, kv_ok, n_tiles are read). The output
-is [N, H', 128] in q's dtype; padding rows are unspecified.
+A backend takes one head group of one layer in tile order and returns its
+attention output: `attend(q, k, v, block_mask, layout)` with q / k / v
+[N, H', 128] (padding slots zero), block_mask [H', n_tiles, n_tiles] bool
+(row = query tile) and a tile layout, of which only valid_count, kv_ok and
+n_tiles are used (this package's TileLayout or the reference's own). The
+result is [N, H', 128] in q's dtype; rows of padding slots carry no
+meaning (base.py:61-77).
 
-Errors follow base.py:28-39: `BackendUnavailable` when the backend cannot
-run here (message shown to the user), `MissingDependency` when the user can
-fix it by building the library. `self_test` is base.py:123-155: the result
-must be within `tolerance` x absmax of fp32 masked attention and must not
-be the dense result.
+Two error types tell the user what happened (base.py:28-39):
+`BackendUnavailable` means this machine cannot run the backend, and
+`MissingDependency` that the user can fix it (here: build the library).
+
+The reference validates a backend with its own `base.self_test` before the
+first call; integration/b200_int8.py is the module that plugs this backend
+into the reference's registry, and the GPU tests run that self-test on it.
 """
 
 from __future__ import annotations
@@ -23,7 +26,6 @@ import torch
 
 from . import _lib
 from . import kernels
-from . import ops
 from . import selection
 from . import tiling
 
@@ -112,8 +114,8 @@ def create(device: torch.device | None = None) -> Backend:
 
 
 def reference_attention(q, k, v, block_mask, layout) -> torch.Tensor:
-    """fp32 masked softmax attention, the self-test's yardstick
-    (core/reference.py:14-36): O(N^2) memory, small problems only."""
+    """fp32 masked softmax attention over the kept tiles, the yardstick of
+    core/reference.py:14-36: O(N^2) memory, small problems only."""
     tile = tiling.TILE_SIZE
     scale = q.shape[-1] ** -0.5
     allowed = block_mask.repeat_interleave(tile, 1).repeat_interleave(tile, 2)
@@ -136,66 +138,3 @@ def mask_from_lists(index: torch.Tensor, count: torch.Tensor,
                        device=index.device)
     mask.scatter_(2, cols, True)
     return mask[..., :n_tiles].contiguous()
-
-
-def selftest_problem(device: torch.device, dtype: torch.dtype, seed: int = 0):
-    """The reference's self-test problem (base.py:94-120): text 70 | history
-    1x8x16 | audio 40 | target 5x8x8 tiled 4x4x8, 2 heads, x ~ 1.5 N(0,1),
-    budgets 2 (generated) / 1 (reference) tiles.
-
-    Returns (q, k, v, block_mask, layout).
-    """
-    spans = [tiling.TiledSpan(70, (1, 8, 16), tiling.TileShape(1, 8, 16)),
-             tiling.TiledSpan(238, (5, 8, 8), tiling.TileShape(4, 4, 8))]
-    seq_len = 238 + 320
-    layout = tiling.build_tile_layout(spans, seq_len, device)
-    generator = torch.Generator().manual_seed(seed)
-    heads, dim = 2, 128
-    x = torch.randn(3, seq_len, heads, dim, generator=generator) * 1.5
-    head_ids = torch.arange(heads, device=device)
-    q, k, v = (tiling.gather_tiles(t.to(device=device, dtype=dtype), layout,
-                                   head_ids) for t in x)
-    scores = torch.randn(heads, layout.n_video_tiles, layout.n_video_tiles,
-                         generator=generator).to(device)
-    blocks = selection.column_blocks(layout, selection.Budget(tiles=2),
-                                     selection.Budget(tiles=1))
-    index, count = selection.select_index(scores, layout, blocks)
-    mask = mask_from_lists(index, count, layout.n_tiles)
-    return q, k, v, mask, layout
-
-
-def self_test(backend: Backend, device: torch.device,
-              dtype: torch.dtype = torch.bfloat16) -> None:
-    """Checks `backend` against fp32 masked attention on `device`.
-
-    Raises:
-        BackendUnavailable: If the result is wrong, dense, or the kernels
-            reported a device-side error.
-    """
-    if dtype not in backend.dtypes:
-        dtype = backend.dtypes[0]
-    try:
-        q, k, v, mask, layout = selftest_problem(device, dtype)
-        out = backend.attend(q, k, v, mask, layout)
-        ops.check_status(device)
-    except BackendUnavailable:
-        raise
-    except Exception as error:  # kernels fail in many ways; report, not crash
-        raise BackendUnavailable(
-            f'{backend.name} failed its self-test: {type(error).__name__}: '
-            f'{error}') from error
-    real = layout.slot_valid.bool()
-    want = reference_attention(q, k, v, mask, layout)[real]
-    dense = reference_attention(q, k, v, torch.ones_like(mask) & layout.kv_ok,
-                                layout)[real]
-    got = out[real].float()
-    err = (got - want).abs().max().item()
-    gap = (dense - want).abs().max().item()
-    if (got - dense).abs().max().item() < 0.5 * gap:
-        raise BackendUnavailable(f'{backend.name} ignores the block mask on '
-                                 'this device (computes dense attention)')
-    limit = backend.tolerance * max(1.0, want.abs().max().item())
-    if not err <= limit:
-        raise BackendUnavailable(f'{backend.name} gives wrong results on this '
-                                 f'device (max error {err:.3g}, allowed '
-                                 f'{limit:.3g})')

@@ -67,7 +67,8 @@ class VedaAttention:
               proj_q: torch.Tensor | None = None,
               proj_k: torch.Tensor | None = None, full: bool = False,
               out: torch.Tensor | None = None,
-              tiled: bool | None = None) -> torch.Tensor:
+              tiled: bool | None = None,
+              out_multicast: int = 0) -> torch.Tensor:
         """Veda attention of one layer.
 
         Args:
@@ -81,12 +82,24 @@ class VedaAttention:
             tiled: Whether q / k / v are already in tile order. By default
                 they are when they have N rows and either the layout is the
                 identity or N differs from the packed length S.
+            out_multicast: Head-sharded output (tile-order inputs only):
+                the NVSwitch multicast address of `out`'s first element,
+                through which the attention kernel writes every row to all
+                GPUs bound to the multicast object (see `sharding`).
 
         Returns:
             Attention output with q's leading shape and v's dtype, in the
             order of the inputs (tile order for tiled inputs).
         """
         heads = q.shape[1]
+        if tiled is None and q.shape[0] not in (layout.num_slots,
+                                                 layout.seq_len):
+            raise ValueError(f'q has {q.shape[0]} rows: expected the '
+                             f'layout\'s {layout.seq_len} packed rows or '
+                             f'{layout.num_slots} tile slots')
+        if tiled is False and q.shape[0] < layout.seq_len:
+            raise ValueError(f'packed q has {q.shape[0]} rows, fewer than '
+                             f'the layout\'s {layout.seq_len}')
         if tiled is None:
             tiled = q.shape[0] == layout.num_slots and (
                 layout.identity or q.shape[0] != layout.seq_len)
@@ -125,9 +138,13 @@ class VedaAttention:
             return ops.sparse_attention(
                 quant['q_i8'], quant['q_scale'], quant['k_i8'],
                 quant['k_scale'], v_t, index, count, layout.valid_count,
-                out=out)
+                out=out, out_multicast=out_multicast)
+        if out_multicast:
+            raise ValueError('a multicast output needs tile-order inputs')
         if out is None:
-            out = torch.zeros(q.shape[0], heads, dim, dtype=v.dtype,
+            # every row of the sequence belongs to a tile slot, so the
+            # kernel writes all of them: no clearing pass
+            out = torch.empty(q.shape[0], heads, dim, dtype=v.dtype,
                               device=q.device)
         return ops.sparse_attention(quant['q_i8'], quant['q_scale'],
                                     quant['k_i8'], quant['k_scale'], v_t,
