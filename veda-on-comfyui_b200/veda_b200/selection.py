@@ -25,23 +25,30 @@ from . import tiling
 
 @dataclasses.dataclass(frozen=True)
 class Budget:
-    """Keep budget of one column block: a keep ratio or a tile count."""
+    """How many key tiles a query tile keeps in one column block.
+
+    Exactly one field is set: `tiles`, a fixed (possibly fractional) number
+    per query tile, or `ratio`, the share of an equal-cost dense budget
+    (1 - sparsity; 1 or more keeps the whole block).
+    """
 
     ratio: float | None = None
     tiles: float | None = None
 
     def __post_init__(self):
         if (self.ratio is None) == (self.tiles is None):
-            raise ValueError('set exactly one of ratio / tiles')
+            raise ValueError('a Budget takes a ratio or a tile count, not '
+                             'both and not neither')
         value = self.ratio if self.tiles is None else self.tiles
         if value <= 0:
-            raise ValueError(f'budget must be positive: {self}')
+            raise ValueError(f'a Budget keeps at least something, got {self}')
 
     @classmethod
     def sparsity(cls, percent: float) -> 'Budget':
-        """Skip `percent` % of the key tiles (keep ratio 1 - percent / 100)."""
+        """The budget that skips `percent` % of the key tiles."""
         if not 0.0 <= percent < 100.0:
-            raise ValueError(f'sparsity must be in [0, 100): {percent}')
+            raise ValueError(f'sparsity is a percentage below 100, got '
+                             f'{percent}')
         return cls(ratio=1.0 - percent / 100.0)
 
     @property
@@ -49,8 +56,10 @@ class Budget:
         return self.ratio is not None and self.ratio >= 1.0
 
     def per_row(self, real_tokens: int, n_cols: int) -> float:
-        """Tiles kept per query tile: the count, or the equal-cost ratio
-        budget ratio * ceil(real / 128)^2 / n_cols."""
+        """Mean tiles kept by one query tile of a block with `n_cols`
+        columns covering `real_tokens` tokens. A ratio is taken of the work
+        the block would cost if its tokens filled whole tiles, ceil(real /
+        128)^2 pairs, spread over its n_cols rows."""
         if self.tiles is not None:
             return float(self.tiles)
         n_ideal = math.ceil(real_tokens / tiling.TILE_SIZE)
@@ -58,8 +67,11 @@ class Budget:
 
 
 def split_budget(budget: float, n_cols: int) -> tuple[int, int, float]:
-    """(k_lo, k_hi, frac) with 1 <= k_lo <= k_hi <= n_cols; frac rounded to
-    12 decimals so 2.3 gives 0.3 exactly as a double."""
+    """A fractional per-row budget as whole tiles: every row keeps k_lo,
+    and a share `frac` of the rows keeps k_hi = k_lo + 1 (both within
+    [1, n_cols]). `frac` is rounded to 12 decimals, so a budget of 2.3
+    yields a fraction that is 0.3 as a double, not 0.29999..., which would
+    change which rows get the extra tile."""
     if budget >= n_cols:
         return n_cols, n_cols, 0.0
     k_lo = min(max(1, math.floor(budget)), n_cols)
@@ -79,14 +91,16 @@ def _bresenham(n_rows: int, frac: float, device: str) -> torch.Tensor:
 
 def bresenham_extra(n_rows: int, frac: float,
                     device: torch.device | str) -> torch.Tensor:
-    """[n_rows] uint8: row r keeps k_hi iff floor((r+1) f) > floor(r f)
-    (fp64, so the mean kept count equals the budget). Cached; read only."""
+    """Which rows take the extra tile: [n_rows] uint8, 1 where the fp64
+    line floor(r * frac) steps up between r and r + 1, which spreads the
+    extras evenly and makes the mean kept count equal the budget. The
+    tensor is cached per device and must not be written."""
     return _bresenham(n_rows, float(frac), str(torch.device(device)))
 
 
 @dataclasses.dataclass(frozen=True)
 class ColumnBlock:
-    """A sparse column block of the video quadrant."""
+    """A range [start, stop) of video key tiles that shares one budget."""
 
     start: int
     stop: int

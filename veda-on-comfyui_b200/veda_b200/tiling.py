@@ -30,7 +30,8 @@ TILE_SIZE = 128
 
 @dataclasses.dataclass(frozen=True, order=True)
 class TileShape:
-    """A (t, h, w) box of TILE_SIZE tokens."""
+    """The extents (t, h, w) of one tile in frames, rows and columns of the
+    latent grid; their product is the tile size, 128."""
 
     t: int
     h: int
@@ -38,20 +39,25 @@ class TileShape:
 
     def __post_init__(self):
         if self.t * self.h * self.w != TILE_SIZE:
-            raise ValueError(f'tile {self} does not hold {TILE_SIZE} tokens')
+            raise ValueError(f'{self.t} x {self.h} x {self.w} is '
+                             f'{self.t * self.h * self.w} tokens; a tile has '
+                             f'{TILE_SIZE}')
 
     def padded_grid(self, grid: Sequence[int]) -> tuple[int, int, int]:
+        """`grid` rounded up, per axis, to a whole number of tiles."""
         return tuple(-(-g // s) * s
                      for g, s in zip(grid, (self.t, self.h, self.w)))
 
     def num_tiles(self, grid: Sequence[int]) -> int:
+        """Tiles that cover `grid`, padding included."""
         tp, hp, wp = self.padded_grid(grid)
         return tp * hp * wp // TILE_SIZE
 
 
 @dataclasses.dataclass(frozen=True)
 class TiledSpan:
-    """Packed rows [start, start + T*H*W), T/H/W row-major, tiled by shape."""
+    """A video span of the packed sequence: T * H * W consecutive rows from
+    `start`, frame-major then row-major, cut into tiles of `shape`."""
 
     start: int
     grid: tuple[int, int, int]
@@ -64,7 +70,10 @@ class TiledSpan:
 
 
 def span_tiles(span: TiledSpan) -> np.ndarray:
-    """[n_tiles, 128] int64 packed row ids of one span, -1 on padding."""
+    """The packed rows of each tile of a span, [n_tiles, 128] int64. Tiles
+    are numbered h-block, w-block, t-block from outer to inner; inside a
+    tile the real rows come first in (t, h, w) order and the padding (-1)
+    last."""
     t, h, w = span.grid
     s = span.shape
     tp, hp, wp = s.padded_grid(span.grid)
