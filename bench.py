@@ -332,6 +332,76 @@ class Call:
         return bool(torch.equal(full, want))
 
 
+def predictor_path(sets: list, device, steps: int, hbm_gbs: float) -> dict:
+    """The scoring half of a real call at cfg1, timed on its own: the
+    quantisation pass with the TripPool features fused in (Q and K read
+    once), the predictor logits from projections staged a layer ahead from
+    pinned host memory (bf16 and fp8 bundle storage), and the top-k
+    selection. CUDA events per phase; medians over `steps` calls, which
+    alternate between two input sets and two layers' projections."""
+    from veda_b200 import kernels, ops, predictor, selection, tiling
+    layout = tiling.identity_layout(REAL, device)
+    blocks = selection.column_blocks(layout, selection.Budget(tiles=KEEP),
+                                     selection.Budget(ratio=1.0))
+    pre = DIM ** -0.5 * kernels.LOG2E
+    g = torch.Generator().manual_seed(77)
+    raw = [[(torch.randn(HEADS, 3 * DIM, DIM, generator=g) * 0.02).to(
+        torch.bfloat16) for _ in range(2)] for _ in range(2)]
+    quant = {}
+    work = torch.empty(2 * N_TILES * HEADS * DIM, dtype=torch.float32,
+                       device=device)
+    out = {}
+    for storage in ('bf16', 'fp8'):
+        if storage == 'fp8':
+            packed = [[predictor.quantize_fp8(w) for w in layer]
+                      for layer in raw]
+            stager = predictor.ProjectionStager(
+                [p[0][0] for p in packed], [p[1][0] for p in packed], device,
+                [p[0][1] for p in packed], [p[1][1] for p in packed])
+        else:
+            stager = predictor.ProjectionStager([r[0] for r in raw],
+                                                [r[1] for r in raw], device)
+        times = []
+        for i in range(steps + 3):
+            s = sets[i % len(sets)]
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record()
+            qp = ops.quant_pool(s['q'], s['k'], layout.valid_count,
+                                layout.n_video_tiles, pre, pool=True,
+                                out=quant)
+            ev[1].record()
+            scores = stager.get(i % 2).logits(qp['feats_q'], qp['feats_k'],
+                                              work)
+            ev[2].record()
+            selection.select_index(scores, layout, blocks)
+            ev[3].record()
+            if i >= 3:
+                times.append(ev)
+        torch.cuda.synchronize(device)
+        ph = np.array([[e[j].elapsed_time(e[j + 1]) for j in range(3)]
+                       for e in times])
+        med = np.median(ph, axis=0)
+        out[storage] = {'pool_quant_ms': float(med[0]),
+                        'logits_ms': float(med[1]),
+                        'select_ms': float(med[2]),
+                        'total_ms': float(med.sum()),
+                        'projection_bytes_per_layer': stager.bytes_per_layer}
+    ops.check_status(device)
+    # algorithmic bytes of the pooled quantisation pass
+    elems = SEQ * HEADS * DIM
+    nbytes = (2 * elems * 2 + 2 * elems + HEADS * N_TILES * 4 * 3
+              + 2 * HEADS * N_TILES * 3 * DIM * 4)
+    gbs = nbytes / (out['bf16']['pool_quant_ms'] * 1e-3) / 1e9
+    out.update({'workload': 'cfg1 scoring: quant_pool (Q, K int8 + TripPool '
+                            'features), predictor logits (24 x 256 x 256, '
+                            '[24, 384, 128] projections per layer staged a '
+                            'layer ahead), top-26 selection',
+                'pool_quant_bytes': nbytes, 'pool_quant_gbs': gbs,
+                'pool_quant_frac_of_hbm': gbs / hbm_gbs,
+                'steps': steps})
+    return out
+
+
 def _reference_cpu_modules():
     """(reference, selection, tiling) of the reference's torch core from the
     unmodified package in baseline/_ref, or None when it is absent."""
@@ -903,6 +973,9 @@ def main():
             'gpu_launches': 3 * args.steps,
             'clocks': clocks.summary(),
         }
+        if world == 1:
+            line['predictor_path'] = predictor_path(
+                sets[:2], device, max(args.steps, 10), peaks['hbm_gbs'])
         if world == 1 and not args.no_cpu_baseline:
             line['cpu_baseline'] = cpu_reference()
         print(json.dumps(line), file=json_out, flush=True)

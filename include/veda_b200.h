@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define VEDA_ABI_VERSION 1
+#define VEDA_ABI_VERSION 2
 
 /* Return codes. */
 #define VEDA_OK 0
@@ -39,6 +39,7 @@ extern "C" {
 #define VEDA_BF16 0
 #define VEDA_F16 1
 #define VEDA_F32 2
+#define VEDA_FP8_E4M3 3 /* predictor projections only, with per-head scales */
 
 /* Version of this ABI (VEDA_ABI_VERSION). */
 int veda_abi_version(void);
@@ -99,6 +100,25 @@ int veda_tile_logits(const float* feats_q, const float* feats_k,
                      const void* proj_q, const void* proj_k, int proj_dtype,
                      int heads, int n_q, int n_k, float* workspace,
                      float* logits, void* stream);
+
+/*
+ * veda_tile_logits for projections stored in fp8 (e4m3) with one fp32 scale
+ * per head, as fp8 predictor bundles keep them.
+ * Replaces core/bundle.py:176-180 (dequantisation at load) and
+ * core/predictor.py:63-80: each weight is used as bf16(w * scale[h]), the
+ * value the reference's loader stores, so the logits equal those of
+ * veda_tile_logits on the dequantised bf16 weights. The fp8 tensors cross
+ * PCIe and HBM at half the bytes of bf16.
+ *   proj_dtype   VEDA_FP8_E4M3 (scale_q / scale_k [heads] fp32 required) or
+ *                any type of veda_tile_logits (scales ignored, may be NULL).
+ * Other arguments as veda_tile_logits.
+ */
+int veda_tile_logits_scaled(const float* feats_q, const float* feats_k,
+                            const void* proj_q, const void* proj_k,
+                            int proj_dtype, const float* scale_q,
+                            const float* scale_k, int heads, int n_q,
+                            int n_k, float* workspace, float* logits,
+                            void* stream);
 
 /* Row limit of veda_tile_logits_static: (n_q + n_k) * heads. */
 #define VEDA_STATIC_LOGITS_ROWS 16384
@@ -222,13 +242,19 @@ int veda_sparse_attention_multicast(
  * strides and that every perm entry is below seq_len: rows at or past
  * seq_len are treated as padding, but seq_len itself is not checked
  * against the tensors (raw pointers carry no extent).
+ *   head_ids     [heads] int32, or NULL for heads 0 .. heads - 1: output
+ *                head h is input head head_ids[h], so one head group of a
+ *                layer (core/plans.py:25-29 HeadGroup; core/engine.py:
+ *                282-297) is quantised without a copy of q[:, group]. The
+ *                caller guarantees every id is a head of q and k.
  */
 int veda_quant_pool_packed(
     const void* q, const void* k, int dtype, int64_t stride_n,
     int64_t stride_h, int64_t seq_len, const int64_t* perm, int n_slots,
     int heads, const int32_t* valid_count, int n_video_tiles,
     float q_pre_scale, int8_t* q_i8, float* q_scale, int8_t* k_i8,
-    float* k_scale, float* feats_q, float* feats_k, void* stream);
+    float* k_scale, float* feats_q, float* feats_k, const int32_t* head_ids,
+    void* stream);
 
 /*
  * veda_sparse_attention with a packed output: row `slot` of the result goes
@@ -238,6 +264,10 @@ int veda_quant_pool_packed(
  * Same bits as veda_sparse_attention followed by veda_scatter_tiles.
  * The caller guarantees that `out` holds seq_len rows at the given strides;
  * slots whose perm entry is at or past seq_len are dropped like padding.
+ *   out_heads    [heads] int32, or NULL for heads 0 .. heads - 1: head h of
+ *                this call is written to head out_heads[h] of `out` (one
+ *                head group of a layer; the caller guarantees every id is
+ *                a head of `out`).
  */
 int veda_sparse_attention_packed(
     const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
@@ -245,7 +275,8 @@ int veda_sparse_attention_packed(
     int64_t v_stride_h, const int32_t* index, int width, const int32_t* count,
     const int32_t* valid_count, int heads, int n_tiles, void* out,
     int64_t out_stride_n, int64_t out_stride_h, const int64_t* perm,
-    int64_t seq_len, int32_t* status, void* stream);
+    int64_t seq_len, const int32_t* out_heads, int32_t* status,
+    void* stream);
 
 /*
  * Tile-order permutation of packed rows (core/tiling.py:227-242,

@@ -88,6 +88,61 @@ def test_pool_and_logits_match_reference_fixture(cuda_device):
                                    rtol=1e-4, atol=1e-5)
 
 
+def test_fp8_projections_equal_the_dequantised_bf16_path(cuda_device):
+    """fp8 bundle storage: the logits from fp8 weights with per-head scales
+    equal, bit for bit, those from the weights the reference's loader makes
+    of them (bf16(w.float() * scale), core/bundle.py:176-180)."""
+    from veda_b200 import predictor
+    case = problems.CASES['gpu_problem']
+    q, k, _, _, _ = problems.make_problem(case)
+    layout = helpers.device_layout(case, cuda_device)
+    proj = problems.make_proj(case)
+    fq = predictor.pool_video_tiles(q.to(cuda_device), layout)
+    fk = predictor.pool_video_tiles(k.to(cuda_device), layout)
+    (wq, sq), (wk, sk) = (predictor.quantize_fp8(p) for p in proj)
+    deq = [(w.float() * s.view(-1, 1, 1)).to(torch.bfloat16)
+           for w, s in ((wq, sq), (wk, sk))]
+    want = predictor.tile_logits(fq, fk, deq[0].to(cuda_device),
+                                 deq[1].to(cuda_device))
+    got = predictor.tile_logits(fq, fk, wq.to(cuda_device),
+                                wk.to(cuda_device), scale_q=sq, scale_k=sk)
+    assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize('storage', ['bf16', 'fp8'])
+def test_projection_stager_serves_every_layer(cuda_device, storage):
+    """Layers fetched through the stager (copies a layer ahead on a side
+    stream, two device slots) give the logits of their own weights, with
+    every layer's work queued before any is read back."""
+    from veda_b200 import predictor
+    case = problems.CASES['gpu_problem']
+    q, k, _, _, _ = problems.make_problem(case)
+    layout = helpers.device_layout(case, cuda_device)
+    fq = predictor.pool_video_tiles(q.to(cuda_device), layout)
+    fk = predictor.pool_video_tiles(k.to(cuda_device), layout)
+    layers = 5
+    raw = [problems.make_proj(case, seed=200 + i) for i in range(layers)]
+    if storage == 'fp8':
+        packed = [[predictor.quantize_fp8(p) for p in r] for r in raw]
+        stager = predictor.ProjectionStager(
+            [p[0][0] for p in packed], [p[1][0] for p in packed],
+            cuda_device, [p[0][1] for p in packed], [p[1][1] for p in packed])
+        direct = [predictor.LayerProjections(
+            p[0][0].to(cuda_device), p[1][0].to(cuda_device),
+            p[0][1].to(cuda_device), p[1][1].to(cuda_device)) for p in packed]
+    else:
+        stager = predictor.ProjectionStager([r[0] for r in raw],
+                                            [r[1] for r in raw], cuda_device)
+        direct = [predictor.LayerProjections(r[0].to(cuda_device),
+                                             r[1].to(cuda_device))
+                  for r in raw]
+    got = [stager.get(i).logits(fq, fk) for i in range(layers)]
+    want = [d.logits(fq, fk) for d in direct]
+    torch.cuda.synchronize(cuda_device)
+    for i in range(layers):
+        assert torch.equal(got[i], want[i]), i
+
+
 # ------------------------------------------------------------------ select
 
 @pytest.mark.parametrize('name', list(problems.CASES))

@@ -106,6 +106,9 @@ struct AttnParams {
   // padding, which is dropped (core/tiling.py:245-252).
   const int64_t* perm;
   int64_t seq_len;
+  // Packed output of one head group (null: all heads): head h of this call
+  // is head out_heads[h] of `out`.
+  const int32_t* out_heads;
   int n_tiles, width, heads;
   int n_pairs;           // heads * ceil(n_tiles / 2)
   int32_t* status;
@@ -567,7 +570,10 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
         dest[i] = d < p.seq_len ? d : -1;
       }
     }
-    VT* packed = static_cast<VT*>(p.out) + static_cast<int64_t>(head) * p.out_sh;
+    const int out_head = p.out_heads != nullptr ? __ldg(p.out_heads + head)
+                                                : head;
+    VT* packed =
+        static_cast<VT*>(p.out) + static_cast<int64_t>(out_head) * p.out_sh;
     if (count == 0) {  // nothing kept: the reference's acc / 1 = 0
       publish();
       float zero[32];
@@ -873,7 +879,8 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
            int width, const int32_t* count, const int32_t* valid_count,
            int heads, int n_tiles, void* out, void* out_mc,
            int64_t out_stride_n, int64_t out_stride_h, int32_t* status,
-           void* stream, const int64_t* perm = nullptr, int64_t seq_len = 0) {
+           void* stream, const int64_t* perm = nullptr, int64_t seq_len = 0,
+           const int32_t* out_heads = nullptr) {
   if (int rc = check_device()) return rc;
   if (perm != nullptr && (seq_len <= 0 || out_mc != nullptr))
     return fail(VEDA_ERR_INVALID,
@@ -952,6 +959,7 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
   p.out_sh = out_stride_h;
   p.perm = perm;
   p.seq_len = seq_len;
+  p.out_heads = out_heads;
   p.n_tiles = n_tiles;
   p.width = width;
   p.heads = heads;
@@ -999,10 +1007,11 @@ extern "C" int veda_sparse_attention_packed(
     int64_t v_stride_h, const int32_t* index, int width, const int32_t* count,
     const int32_t* valid_count, int heads, int n_tiles, void* out,
     int64_t out_stride_n, int64_t out_stride_h, const int64_t* perm,
-    int64_t seq_len, int32_t* status, void* stream) {
+    int64_t seq_len, const int32_t* out_heads, int32_t* status,
+    void* stream) {
   if (perm == nullptr) return fail(VEDA_ERR_INVALID, "null perm");
   return attend(q_i8, q_scale, k_i8, k_scale, v, v_dtype, v_stride_n,
                 v_stride_h, index, width, count, valid_count, heads, n_tiles,
                 out, nullptr, out_stride_n, out_stride_h, status, stream, perm,
-                seq_len);
+                seq_len, out_heads);
 }

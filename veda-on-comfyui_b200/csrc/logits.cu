@@ -5,6 +5,8 @@
 // anything worth a tensor-core pipeline, and fp32 keeps the logits (and so
 // the selection) within rounding of the reference's fp32 bmm.
 
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace veda {
@@ -26,13 +28,32 @@ template <>
 __device__ __forceinline__ float to_f<__half>(__half v) {
   return __half2float(v);
 }
+template <>
+__device__ __forceinline__ float to_f<__nv_fp8_e4m3>(__nv_fp8_e4m3 v) {
+  return static_cast<float>(v);
+}
+
+// A projection weight as the scoring arithmetic sees it. fp8 weights carry a
+// per-head scale and become bf16(w * scale) in fp32, which is what the
+// reference's bundle loader stores for them (core/bundle.py:176-180: the
+// fp32 product rounded to bf16) before its fp32 bmm.
+template <typename PT>
+__device__ __forceinline__ float weight(PT v, float scale) {
+  return to_f(v);
+}
+template <>
+__device__ __forceinline__ float weight<__nv_fp8_e4m3>(__nv_fp8_e4m3 v,
+                                                      float scale) {
+  return __bfloat162float(__float2bfloat16_rn(to_f(v) * scale));
+}
 
 // grid (ceil(n / 16), heads, 2): z = 0 projects q features, z = 1 k.
+// sq / sk: per-head scales of fp8 projections (unused otherwise).
 template <typename PT>
 __global__ void __launch_bounds__(256)
     project_kernel(const float* fq, const float* fk, const PT* pq,
-                   const PT* pk, int n_q, int n_k, float* hat_q,
-                   float* hat_k) {
+                   const PT* pk, const float* sq, const float* sk, int n_q,
+                   int n_k, float* hat_q, float* hat_k) {
   __shared__ float f_sh[kProjRows][kFeat];
   const bool is_k = blockIdx.z == 1;
   const int n = is_k ? n_k : n_q;
@@ -41,6 +62,8 @@ __global__ void __launch_bounds__(256)
   if (row0 >= n) return;
   const float* f = (is_k ? fk : fq) + (static_cast<int64_t>(head) * n + row0) * kFeat;
   const PT* proj = (is_k ? pk : pq) + static_cast<int64_t>(head) * kFeat * kDim;
+  const float* scales = is_k ? sk : sq;
+  const float scale = scales != nullptr ? scales[head] : 1.0f;
   float* out = (is_k ? hat_k : hat_q) + (static_cast<int64_t>(head) * n + row0) * kDim;
   const int rows = min(kProjRows, n - row0);
   for (int i = threadIdx.x; i < kProjRows * kFeat; i += blockDim.x) {
@@ -54,7 +77,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int r = 0; r < kProjRows / 2; ++r) acc[r] = 0.0f;
   for (int k = 0; k < kFeat; ++k) {
-    const float w = to_f(proj[static_cast<int64_t>(k) * kDim + d]);
+    const float w = weight(proj[static_cast<int64_t>(k) * kDim + d], scale);
 #pragma unroll
     for (int r = 0; r < kProjRows / 2; ++r)
       acc[r] = fmaf(f_sh[r0 + r][k], w, acc[r]);
@@ -132,8 +155,9 @@ int check_logits_args(const float* feats_q, const float* feats_k,
 
 int launch_tile_logits(const float* feats_q, const float* feats_k,
                        const void* proj_q, const void* proj_k, int proj_dtype,
-                       int heads, int n_q, int n_k, float* workspace,
-                       float* logits, cudaStream_t s) {
+                       const float* scale_q, const float* scale_k, int heads,
+                       int n_q, int n_k, float* workspace, float* logits,
+                       cudaStream_t s) {
   float* hat_q = workspace;
   float* hat_k = workspace + static_cast<int64_t>(heads) * n_q * kDim;
   const int n_max = n_q > n_k ? n_q : n_k;
@@ -142,20 +166,32 @@ int launch_tile_logits(const float* feats_q, const float* feats_k,
     case VEDA_BF16:
       project_kernel<__nv_bfloat16><<<pgrid, 256, 0, s>>>(
           feats_q, feats_k, static_cast<const __nv_bfloat16*>(proj_q),
-          static_cast<const __nv_bfloat16*>(proj_k), n_q, n_k, hat_q, hat_k);
+          static_cast<const __nv_bfloat16*>(proj_k), nullptr, nullptr, n_q,
+          n_k, hat_q, hat_k);
       break;
     case VEDA_F16:
       project_kernel<__half><<<pgrid, 256, 0, s>>>(
           feats_q, feats_k, static_cast<const __half*>(proj_q),
-          static_cast<const __half*>(proj_k), n_q, n_k, hat_q, hat_k);
+          static_cast<const __half*>(proj_k), nullptr, nullptr, n_q, n_k,
+          hat_q, hat_k);
       break;
     case VEDA_F32:
       project_kernel<float><<<pgrid, 256, 0, s>>>(
           feats_q, feats_k, static_cast<const float*>(proj_q),
-          static_cast<const float*>(proj_k), n_q, n_k, hat_q, hat_k);
+          static_cast<const float*>(proj_k), nullptr, nullptr, n_q, n_k,
+          hat_q, hat_k);
+      break;
+    case VEDA_FP8_E4M3:
+      if (scale_q == nullptr || scale_k == nullptr)
+        return fail(VEDA_ERR_INVALID, "fp8 projections need per-head scales");
+      project_kernel<__nv_fp8_e4m3><<<pgrid, 256, 0, s>>>(
+          feats_q, feats_k, static_cast<const __nv_fp8_e4m3*>(proj_q),
+          static_cast<const __nv_fp8_e4m3*>(proj_k), scale_q, scale_k, n_q,
+          n_k, hat_q, hat_k);
       break;
     default:
-      return fail(VEDA_ERR_INVALID, "proj dtype must be bf16, fp16 or fp32");
+      return fail(VEDA_ERR_INVALID,
+                  "proj dtype must be bf16, fp16, fp32 or fp8 e4m3");
   }
   VEDA_CHECK_CUDA(cudaGetLastError());
   dim3 lgrid((n_k + kLogitTile - 1) / kLogitTile,
@@ -180,9 +216,29 @@ extern "C" int veda_tile_logits(const float* feats_q, const float* feats_k,
                                  n_k, logits))
     return rc;
   if (workspace == nullptr) return fail(VEDA_ERR_INVALID, "null workspace");
+  if (proj_dtype == VEDA_FP8_E4M3)
+    return fail(VEDA_ERR_INVALID,
+                "fp8 projections go through veda_tile_logits_scaled");
   return launch_tile_logits(feats_q, feats_k, proj_q, proj_k, proj_dtype,
-                            heads, n_q, n_k, workspace, logits,
-                            static_cast<cudaStream_t>(stream));
+                            nullptr, nullptr, heads, n_q, n_k, workspace,
+                            logits, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int veda_tile_logits_scaled(const float* feats_q,
+                                       const float* feats_k,
+                                       const void* proj_q, const void* proj_k,
+                                       int proj_dtype, const float* scale_q,
+                                       const float* scale_k, int heads,
+                                       int n_q, int n_k, float* workspace,
+                                       float* logits, void* stream) {
+  if (int rc = check_device()) return rc;
+  if (int rc = check_logits_args(feats_q, feats_k, proj_q, proj_k, heads, n_q,
+                                 n_k, logits))
+    return rc;
+  if (workspace == nullptr) return fail(VEDA_ERR_INVALID, "null workspace");
+  return launch_tile_logits(feats_q, feats_k, proj_q, proj_k, proj_dtype,
+                            scale_q, scale_k, heads, n_q, n_k, workspace,
+                            logits, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int veda_tile_logits_static(const float* feats_q,
@@ -205,7 +261,10 @@ extern "C" int veda_tile_logits_static(const float* feats_q,
   if (int rc = check_device()) return rc;
   float* scratch = nullptr;
   if (int rc = static_scratch(&scratch)) return rc;
+  if (proj_dtype == VEDA_FP8_E4M3)
+    return fail(VEDA_ERR_INVALID,
+                "fp8 projections go through veda_tile_logits_scaled");
   return launch_tile_logits(feats_q, feats_k, proj_q, proj_k, proj_dtype,
-                            heads, n_q, n_k, scratch, logits,
-                            static_cast<cudaStream_t>(stream));
+                            nullptr, nullptr, heads, n_q, n_k, scratch,
+                            logits, static_cast<cudaStream_t>(stream));
 }

@@ -38,6 +38,9 @@ struct QuantParams {
   // < 0 for padding, which reads as zeros (core/tiling.py:227-242).
   const int64_t* perm;
   int64_t seq_len;
+  // Head group (null: all heads): output head h reads input head heads[h],
+  // so one head group of a layer is quantised without copying it out.
+  const int32_t* heads;
 };
 
 // Eight 16-bit values of one 16-byte load, widened to fp32 (exact).
@@ -91,8 +94,9 @@ __global__ void __launch_bounds__(kQuantThreads, POOL ? 2 : 3)
   const int dc = tid & 15;  // dims 8*dc .. 8*dc+7
   const int rg = tid >> 4;  // rows rg + 16 i
 
+  const int src_head = p.heads != nullptr ? __ldg(p.heads + head) : head;
   const T* x = static_cast<const T*>(job.x) +
-               static_cast<int64_t>(head) * p.stride_h + 8 * dc;
+               static_cast<int64_t>(src_head) * p.stride_h + 8 * dc;
   uint4 raw[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -292,7 +296,8 @@ int quant_pool(const void* q, const void* k, int dtype, int64_t stride_n,
                const int32_t* valid_count, int n_video_tiles,
                float q_pre_scale, int8_t* q_i8, float* q_scale, int8_t* k_i8,
                float* k_scale, float* feats_q, float* feats_k,
-               const int64_t* perm, int64_t seq_len, void* stream) {
+               const int64_t* perm, int64_t seq_len, const int32_t* head_ids,
+               void* stream) {
   if (int rc = check_device()) return rc;
   // packed inputs have seq_len rows; the check wants a whole number of tiles
   const int rows = perm == nullptr ? n_slots : kTile;
@@ -326,6 +331,7 @@ int quant_pool(const void* q, const void* k, int dtype, int64_t stride_n,
   p.n_video = feats_q != nullptr ? n_video_tiles : 0;
   p.perm = perm;
   p.seq_len = seq_len;
+  p.heads = head_ids;
   return launch_quant(p, 2, heads, dtype, static_cast<cudaStream_t>(stream));
 }
 
@@ -340,7 +346,8 @@ extern "C" int veda_quant_pool(const void* q, const void* k, int dtype,
                                void* stream) {
   return quant_pool(q, k, dtype, stride_n, stride_h, n_slots, heads,
                     valid_count, n_video_tiles, q_pre_scale, q_i8, q_scale,
-                    k_i8, k_scale, feats_q, feats_k, nullptr, 0, stream);
+                    k_i8, k_scale, feats_q, feats_k, nullptr, 0, nullptr,
+                    stream);
 }
 
 extern "C" int veda_quant_pool_packed(
@@ -348,9 +355,11 @@ extern "C" int veda_quant_pool_packed(
     int64_t stride_h, int64_t seq_len, const int64_t* perm, int n_slots,
     int heads, const int32_t* valid_count, int n_video_tiles,
     float q_pre_scale, int8_t* q_i8, float* q_scale, int8_t* k_i8,
-    float* k_scale, float* feats_q, float* feats_k, void* stream) {
+    float* k_scale, float* feats_q, float* feats_k, const int32_t* head_ids,
+    void* stream) {
   if (perm == nullptr) return fail(VEDA_ERR_INVALID, "null perm");
   return quant_pool(q, k, dtype, stride_n, stride_h, n_slots, heads,
                     valid_count, n_video_tiles, q_pre_scale, q_i8, q_scale,
-                    k_i8, k_scale, feats_q, feats_k, perm, seq_len, stream);
+                    k_i8, k_scale, feats_q, feats_k, perm, seq_len, head_ids,
+                    stream);
 }

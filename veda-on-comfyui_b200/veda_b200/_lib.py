@@ -20,7 +20,7 @@ STATUS_BAD_INDEX = 2
 STATUS_OVERFLOW = 4
 STATUS_BAD_COUNT = 8
 STATUS_MISALIGNED = 16
-BF16, F16, F32 = 0, 1, 2
+BF16, F16, F32, FP8_E4M3 = 0, 1, 2, 3
 
 _STATUS_NAMES = {STATUS_TIMEOUT: 'a bounded wait timed out',
                  STATUS_BAD_INDEX: 'a tile id was out of range',
@@ -66,6 +66,8 @@ SIGNATURES = {
     'veda_quant_pool': [_P, _P, _I, _L, _L, _I, _I, _P, _I, _F, _P, _P, _P,
                         _P, _P, _P, _P],
     'veda_tile_logits': [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P],
+    'veda_tile_logits_scaled': [_P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _P,
+                                _P, _P],
     'veda_tile_logits_static': [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P],
     'veda_select': [_P, _L, _L, _I, _I, _I, _P, _I,
                     ctypes.POINTER(ColumnBlock), _P, _I, _P, _P, _P, _P],
@@ -76,10 +78,10 @@ SIGNATURES = {
                                         _I, _P, _P, _I, _I, _P, _P, _L, _L,
                                         _P, _P],
     'veda_quant_pool_packed': [_P, _P, _I, _L, _L, _L, _P, _I, _I, _P, _I,
-                               _F, _P, _P, _P, _P, _P, _P, _P],
+                               _F, _P, _P, _P, _P, _P, _P, _P, _P],
     'veda_sparse_attention_packed': [_P, _P, _P, _P, _P, _I, _L, _L, _P, _I,
                                      _P, _P, _I, _I, _P, _L, _L, _P, _L, _P,
-                                     _P],
+                                     _P, _P],
     'veda_gather_tiles': [_P, _I, _L, _L, _I, _I, _P, _I, _P, _I, _P, _P],
     'veda_scatter_tiles': [_P, _I, _P, _I, _P, _I, _I, _P, _L, _L, _I, _P],
 }

@@ -110,16 +110,31 @@ def quantize(x: torch.Tensor, block: int, pre_scale: float = 1.0):
     return out, scale
 
 
+def head_ids(heads, n_heads: int, device: torch.device) -> torch.Tensor:
+    """A head group's ids as the kernels take them: [H'] int32 on `device`,
+    each checked (on the host, before any launch) to be a head of an input
+    with `n_heads` heads."""
+    ids = torch.as_tensor(heads).reshape(-1)
+    if ids.device.type != 'cpu':
+        ids = ids.cpu()
+    if ids.numel() == 0 or int(ids.min()) < 0 or int(ids.max()) >= n_heads:
+        raise ValueError(f'head ids must lie in [0, {n_heads})')
+    return ids.to(device=device, dtype=torch.int32)
+
+
 def quant_pool(q: torch.Tensor, k: torch.Tensor, valid_count: torch.Tensor,
                n_video_tiles: int, q_pre_scale: float, pool: bool = True,
                out: dict | None = None,
-               perm: torch.Tensor | None = None) -> dict:
+               perm: torch.Tensor | None = None,
+               heads: torch.Tensor | None = None) -> dict:
     """Fused INT8 quantisation of Q (per 128 rows) and K (per 64 rows) and,
     if `pool`, the [mean | max | min] features of the video tiles.
 
     perm: packed input. q and k are then [S, H, 128] in sequence order and
     tile slot i reads row perm[i] (< 0: padding, zeros): the gather into
     tile order happens in the same read.
+    heads: with `perm`, one head group: [H'] int32 device ids (see
+    `head_ids`); output head h holds input head heads[h].
 
     Returns dict(q_i8, q_scale, k_i8, k_scale, feats_q, feats_k) in tile
     order; buffers in `out` with those names are reused.
@@ -129,7 +144,15 @@ def quant_pool(q: torch.Tensor, k: torch.Tensor, valid_count: torch.Tensor,
     if q.shape != k.shape or q.stride() != k.stride() or q.dtype != k.dtype:
         raise ValueError('q and k must share shape, strides and dtype')
     device = require_device(q, k, valid_count)
-    seq_len, heads, _ = q.shape
+    seq_len, n_in, _ = q.shape
+    head_map = heads
+    heads = n_in
+    if head_map is not None:
+        if perm is None:
+            raise ValueError('a head group needs packed inputs (perm)')
+        if head_map.dtype != torch.int32 or head_map.device != device:
+            raise ValueError('heads must be int32 ids on the inputs\' device')
+        heads = head_map.numel()
     if perm is not None:
         perm = perm.to(device=device, dtype=torch.int64).contiguous()
     n = seq_len if perm is None else perm.numel()
@@ -163,31 +186,50 @@ def quant_pool(q: torch.Tensor, k: torch.Tensor, valid_count: torch.Tensor,
     else:
         _call(device, 'veda_quant_pool_packed', _ptr(q), _ptr(k),
               _DTYPES[q.dtype], q.stride(0), q.stride(1), seq_len, _ptr(perm),
-              n, heads, *tail)
+              n, heads, *tail[:-1], _ptr(head_map), tail[-1])
     out['feats_q'], out['feats_k'] = feats_q, feats_k
     return out
 
 
 def tile_logits(feats_q: torch.Tensor, feats_k: torch.Tensor,
                 proj_q: torch.Tensor, proj_k: torch.Tensor,
-                workspace: torch.Tensor | None = None) -> torch.Tensor:
+                workspace: torch.Tensor | None = None,
+                scale_q: torch.Tensor | None = None,
+                scale_k: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
     """[H, n_q, 384] x [H, n_k, 384] with [H, 384, 128] projections ->
-    [H, n_q, n_k] fp32 logits."""
+    [H, n_q, n_k] fp32 logits.
+
+    Projections are bf16, fp16, fp32, or fp8 (float8_e4m3fn) with per-head
+    fp32 scales `scale_q` / `scale_k` [H], used as bf16(w * scale) like the
+    reference's bundle loader stores them.
+    """
     device = require_device(feats_q, feats_k, proj_q, proj_k)
     heads, n_q, _ = feats_q.shape
     n_k = feats_k.shape[1]
     feats_q = feats_q.float().contiguous()
     feats_k = feats_k.float().contiguous()
     if proj_q.dtype != proj_k.dtype:
-        proj_k = proj_k.to(proj_q.dtype)
+        raise ValueError('proj_q and proj_k must share a dtype')
     proj_q, proj_k = proj_q.contiguous(), proj_k.contiguous()
+    fp8 = proj_q.dtype == torch.float8_e4m3fn
+    if fp8:
+        if scale_q is None or scale_k is None:
+            raise ValueError('fp8 projections need per-head scales')
+        scale_q = scale_q.to(device=device, dtype=torch.float32).contiguous()
+        scale_k = scale_k.to(device=device, dtype=torch.float32).contiguous()
+        dtype = _lib.FP8_E4M3
+    else:
+        dtype = _DTYPES[proj_q.dtype]
+        scale_q = scale_k = None
     need = (n_q + n_k) * heads * HEAD_DIM
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(need, dtype=torch.float32, device=device)
-    logits = torch.empty(heads, n_q, n_k, dtype=torch.float32, device=device)
-    _call(device, 'veda_tile_logits', _ptr(feats_q), _ptr(feats_k), _ptr(proj_q),
-              _ptr(proj_k), _DTYPES[proj_q.dtype], heads, n_q, n_k,
-              _ptr(workspace), _ptr(logits), _stream(device))
+    logits = out if out is not None else torch.empty(
+        heads, n_q, n_k, dtype=torch.float32, device=device)
+    _call(device, 'veda_tile_logits_scaled', _ptr(feats_q), _ptr(feats_k),
+          _ptr(proj_q), _ptr(proj_k), dtype, _ptr(scale_q), _ptr(scale_k),
+          heads, n_q, n_k, _ptr(workspace), _ptr(logits), _stream(device))
     return logits
 
 
@@ -235,7 +277,8 @@ def mask_to_index(mask: torch.Tensor, kv_ok: torch.Tensor, width: int):
 def sparse_attention(q_i8, q_scale, k_i8, k_scale, v, index, count,
                      valid_count, out: torch.Tensor | None = None,
                      out_multicast: int = 0,
-                     perm: torch.Tensor | None = None):
+                     perm: torch.Tensor | None = None,
+                     heads: torch.Tensor | None = None):
     """INT8 block-sparse attention. v [N, H, 128] 16-bit; returns out
     [N, H, 128] of v's dtype (or writes `out`, any row / head strides).
 
@@ -245,9 +288,12 @@ def sparse_attention(q_i8, q_scale, k_i8, k_scale, v, index, count,
     perm: packed output. `out` ([S, H, 128], required) receives row `slot`
     of the result at row perm[slot]; padding slots (perm < 0) are dropped:
     the scatter back to sequence order happens in the kernel's epilogue.
+    heads: with `perm`, one head group: head h of v / the lists is written to
+    head heads[h] of `out` ([H'] int32 device ids, see `head_ids`).
     """
     _check_rows(v, 'v')
     device = require_device(q_i8, k_i8, v, index, count, valid_count)
+    head_map = heads
     n, heads, _ = v.shape
     n_tiles = n // TILE
     if perm is not None and (out is None or out_multicast):
@@ -257,11 +303,19 @@ def sparse_attention(q_i8, q_scale, k_i8, k_scale, v, index, count,
     _check_rows(out, 'out')
     if out.dtype != v.dtype:
         raise ValueError('out must have v\'s dtype')
+    if head_map is not None and perm is None:
+        raise ValueError('a head group needs a packed output (perm)')
     if perm is not None:
         perm = perm.to(device=device, dtype=torch.int64).contiguous()
-        if perm.numel() != n or out.shape[1] != heads:
-            raise ValueError('perm must have a slot per row of v, and out '
-                             'v\'s heads')
+        if head_map is not None:
+            if head_map.dtype != torch.int32 or head_map.device != device or \
+                    head_map.numel() != v.shape[1]:
+                raise ValueError('heads must be int32 ids on the device, one '
+                                 'per head of v')
+        elif out.shape[1] != v.shape[1]:
+            raise ValueError('out must have v\'s heads')
+        if perm.numel() != n:
+            raise ValueError('perm must have a slot per row of v')
     index = index.to(torch.int32).contiguous()
     count = count.to(torch.int32).contiguous()
     valid = valid_count.to(torch.int32).contiguous()
@@ -276,7 +330,8 @@ def sparse_attention(q_i8, q_scale, k_i8, k_scale, v, index, count,
               ctypes.c_void_p(out_multicast), *tail)
     elif perm is not None:
         _call(device, 'veda_sparse_attention_packed', *head, out.stride(0),
-              out.stride(1), _ptr(perm), out.shape[0], *tail[2:])
+              out.stride(1), _ptr(perm), out.shape[0], _ptr(head_map),
+              *tail[2:])
     else:
         _call(device, 'veda_sparse_attention', *head, *tail)
     return out

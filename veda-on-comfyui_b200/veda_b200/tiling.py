@@ -101,6 +101,7 @@ class TileLayout:
     kv_ok: torch.Tensor           # [n_tiles] bool
     slot_valid: torch.Tensor      # [N] int32
     identity: bool = False        # perm is 0..N-1 over real rows
+    n_global_ok: int = 0          # non-empty global tiles (host copy)
 
     @property
     def n_tiles(self) -> int:
@@ -124,7 +125,8 @@ def _layout(perm: np.ndarray, n_video: int, n_ref: int, n_global: int,
         ref_tokens=ref_tokens, target_tokens=target_tokens, seq_len=seq_len,
         kv_ok=torch.from_numpy(valid > 0).to(device),
         slot_valid=torch.from_numpy(real.astype(np.int32)).to(device),
-        identity=identity and bool(real[:real.sum()].all()))
+        identity=identity and bool(real[:real.sum()].all()),
+        n_global_ok=int((valid[n_video:] > 0).sum()))
 
 
 def build_tile_layout(spans: Sequence[TiledSpan], seq_len: int,
