@@ -240,6 +240,8 @@ class Call:
             self.layout, self.blocks, device)
         self.width = selection.list_width(self.layout, self.blocks)
         self.device = device
+        self.n_local = n_local
+        self.local = None
         self.group, self.world = group, world
         self.quant = {}
         self.pre = DIM ** -0.5 * kernels.LOG2E
@@ -277,7 +279,10 @@ class Call:
                                     f'{self.mc_error})' if self.mc_error
                                     else '')
 
-    def __call__(self, s: dict, events=None):
+    def __call__(self, s: dict, events=None, exchange: bool = True):
+        """One call; `exchange=False` leaves out the output exchange (the
+        kernel writes this rank's heads locally), for the compute-only
+        scaling figure."""
         from veda_b200 import ops
         rec = (lambda i: events[i].record()) if events else (lambda i: None)
         rec(0)
@@ -288,6 +293,18 @@ class Call:
         quant = ops.quant_pool(s['q'], s['k'], self.layout.valid_count, 0,
                                self.pre, pool=False, out=self.quant)
         rec(2)
+        if not exchange:
+            if self.local is None:
+                self.local = torch.empty(SEQ, self.n_local, DIM,
+                                         dtype=torch.bfloat16,
+                                         device=self.device)
+            ops.sparse_attention(quant['q_i8'], quant['q_scale'],
+                                 quant['k_i8'], quant['k_scale'], s['v'],
+                                 index, count, self.layout.valid_count,
+                                 out=self.local)
+            rec(3)
+            rec(4)
+            return count
         ops.sparse_attention(quant['q_i8'], quant['q_scale'], quant['k_i8'],
                              quant['k_scale'], s['v'], index, count,
                              self.layout.valid_count, out=self.out,
@@ -850,6 +867,21 @@ def main():
     total_ms = start.elapsed_time(end)
     phases = np.array([[e[j].elapsed_time(e[j + 1]) for j in range(4)]
                        for e in events])             # steps x 4
+    compute_ms = None
+    if world > 1:
+        # the same steps without the output exchange: compute-only scaling
+        for i in range(args.warmup):
+            call(sets[i % n_sets], exchange=False)
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        c0.record()
+        for i in range(args.steps):
+            call(sets[i % n_sets], exchange=False)
+        c1.record()
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        compute_ms = c0.elapsed_time(c1) / args.steps
     work_pairs = sum(pairs[i % n_sets] for i in range(args.steps))
 
     # ---- e2e: host buffers in, result out, inside the timed region,
@@ -911,8 +943,9 @@ def main():
 
     # ---- max over ranks
     stats = torch.tensor([total_ms / args.steps, e2e_ms,
-                          *phases.mean(0).tolist()], dtype=torch.float64,
-                         device=device)
+                          *phases.mean(0).tolist(),
+                          compute_ms if compute_ms is not None else 0.0],
+                         dtype=torch.float64, device=device)
     sums = torch.tensor([float(work_pairs), float(pairs[0]), float(h2d),
                          float(d2h)], dtype=torch.float64, device=device)
     if world > 1:
@@ -920,6 +953,7 @@ def main():
         torch.distributed.all_reduce(sums, torch.distributed.ReduceOp.SUM)
     ms_step, e2e_ms = float(stats[0]), float(stats[1])
     select_ms, quant_ms, attn_ms, gather_ms = (float(x) for x in stats[2:6])
+    compute_ms = float(stats[6]) if world > 1 else None
     total_pairs, e2e_pairs, h2d_all, d2h_all = (float(x) for x in sums)
 
     if rank == 0:
@@ -971,6 +1005,13 @@ def main():
                                'call (H2D and D2H streams); each call '
                                'moves all of its own bytes'},
             'gpu_launches': 3 * args.steps,
+            **({'compute_only': {
+                'ms_per_step': compute_ms,
+                'value': ops_step / (compute_ms * 1e-3) / 1e12,
+                'unit': 'TFLOPS',
+                'note': 'the same steps with each rank writing its heads '
+                        'locally: no multicast store, no all-gather (max '
+                        'over ranks)'}} if compute_ms else {}),
             'clocks': clocks.summary(),
         }
         if world == 1:

@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define VEDA_ABI_VERSION 2
+#define VEDA_ABI_VERSION 3
 
 /* Return codes. */
 #define VEDA_OK 0
@@ -257,11 +257,20 @@ int veda_quant_pool_packed(
     void* stream);
 
 /*
- * veda_sparse_attention with a packed output: row `slot` of the result goes
- * to row perm[slot] of `out` ([seq_len, heads, 128], any row and head
- * strides), padding slots (perm < 0) are dropped, so the scatter of
- * core/tiling.py:245-252 (scatter_tiles_) happens in the kernel's epilogue.
- * Same bits as veda_sparse_attention followed by veda_scatter_tiles.
+ * veda_sparse_attention on packed rows: V is read and the output written
+ * in sequence order through the tile permutation, so neither the gather of
+ * V (core/tiling.py:227-242) nor the scatter of the output (:245-252,
+ * scatter_tiles_) is a pass of its own.
+ *   v            [seq_len, heads_total, 128] 16-bit with evenly spaced rows
+ *                (v_stride_n a multiple of v_stride_h; heads_total =
+ *                v_stride_n / v_stride_h); slot i of the tile order reads
+ *                row perm[i] (padding slots, perm < 0, read zeros), head
+ *                out_heads[h] (or h).
+ *   out          row `slot` of the result goes to row perm[slot] of `out`
+ *                ([seq_len, heads, 128], any row and head strides); padding
+ *                slots are dropped.
+ * Same bits as veda_gather_tiles of V, veda_sparse_attention and
+ * veda_scatter_tiles.
  * The caller guarantees that `out` holds seq_len rows at the given strides;
  * slots whose perm entry is at or past seq_len are dropped like padding.
  *   out_heads    [heads] int32, or NULL for heads 0 .. heads - 1: head h of
@@ -277,6 +286,25 @@ int veda_sparse_attention_packed(
     int64_t out_stride_n, int64_t out_stride_h, const int64_t* perm,
     int64_t seq_len, const int32_t* out_heads, int32_t* status,
     void* stream);
+
+/*
+ * Diagnostic form of veda_sparse_attention for testing its failure path
+ * without a GPU fault; it has no counterpart in the reference. Every
+ * bounded wait of the kernel gives up after `wait_ns` (0 < wait_ns <= the
+ * 2 s the other entry points use), and with `withhold_first_k_load` set the
+ * first CTA never issues its first K tile load, so the wait for that tile
+ * runs out: the kernel then sets VEDA_STATUS_TIMEOUT in `status`, lets the
+ * copies it did issue land, frees its tensor memory and returns, and the
+ * device stays usable. With withhold_first_k_load = 0 it computes exactly
+ * what veda_sparse_attention computes.
+ */
+int veda_debug_sparse_attention(
+    const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
+    const float* k_scale, const void* v, int v_dtype, int64_t v_stride_n,
+    int64_t v_stride_h, const int32_t* index, int width, const int32_t* count,
+    const int32_t* valid_count, int heads, int n_tiles, void* out,
+    int64_t out_stride_n, int64_t out_stride_h, uint64_t wait_ns,
+    int withhold_first_k_load, int32_t* status, void* stream);
 
 /*
  * Tile-order permutation of packed rows (core/tiling.py:227-242,

@@ -42,7 +42,7 @@ def _ctype(param: str):
         return ctypes.c_void_p
     kind = param.rsplit(' ', 1)[0].replace('const ', '').strip()
     return {'int': ctypes.c_int, 'int64_t': ctypes.c_int64,
-            'float': ctypes.c_float}[kind]
+            'uint64_t': ctypes.c_uint64, 'float': ctypes.c_float}[kind]
 
 
 @pytest.fixture(scope='module')

@@ -109,8 +109,17 @@ struct AttnParams {
   // Packed output of one head group (null: all heads): head h of this call
   // is head out_heads[h] of `out`.
   const int32_t* out_heads;
+  // Packed V (null: V in tile order): V rows are read through this same
+  // permutation from a [seq_len * v_heads, 128] view of [seq_len, v_heads,
+  // 128]; v_rows = seq_len * v_heads is the out-of-range row of padding.
+  const int64_t* v_perm;
+  int v_heads, v_rows;
   int n_tiles, width, heads;
   int n_pairs;           // heads * ceil(n_tiles / 2)
+  uint64_t wait_ns;      // bound of every wait (kWaitLimitNs in production)
+  // Diagnostic only (veda_debug_sparse_attention): CTA 0 never issues its
+  // first K load, so the wait for it runs out and the timeout path runs.
+  int withhold_first_k;
   int32_t* status;
 };
 
@@ -170,12 +179,12 @@ __device__ __forceinline__ Pair decode_pair(int w, const AttnParams& p) {
 // Bounded wait that ignores the abort flag: used to drain copies and MMAs
 // this CTA issued before it exits.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity,
-                                           int32_t* status) {
+                                           const AttnParams& p) {
   if (mbar_try_wait(bar, parity)) return;
   const uint64_t start = global_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - start > kWaitLimitNs) {
-      report(status, VEDA_STATUS_TIMEOUT);
+    if (global_ns() - start > p.wait_ns) {
+      report(p.status, VEDA_STATUS_TIMEOUT);
       return;
     }
   }
@@ -189,70 +198,129 @@ __device__ __forceinline__ uint8_t* q_tile(uint8_t* smem, int slot, int buf) {
   return smem + kSmemQ + (2 * slot + buf) * kQBytes;
 }
 
-// Warp 0, one thread: Q tiles per pair, then K / V tiles in the order the
-// MMA thread consumes them (A and B interleaved, tile by tile).
+// TMA gather of four rows (row coordinates y0..y3 of a 2D map with a box one
+// row high) into consecutive 128-byte rows at `dst`; the 128-byte swizzle
+// depends on the shared-memory address only, so the rows land exactly as a
+// tiled load of the same rows in order would put them.
+__device__ __forceinline__ void tma_gather4(const CUtensorMap* map, void* dst,
+                                            uint64_t* bar, int x, int y0,
+                                            int y1, int y2, int y3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4."
+      "mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
+      : "memory");
+}
+
+// Warp 0: Q tiles per pair, then K / V tiles in the order the MMA thread
+// consumes them (A and B interleaved, tile by tile). Lane 0 waits for the
+// ring stages and issues the Q, K and tile-order V loads. A packed V (one
+// head group of [seq_len, heads, 128] rows, read through the tile
+// permutation) is gathered by the whole warp: lane l brings rows 4 l .. 4 l
+// + 3 of the tile, both 64-column halves, and padding slots read an
+// out-of-range row, which the TMA fills with zeros.
 __device__ void produce(const CUtensorMap* qm, const CUtensorMap* km,
                         const CUtensorMap* vm, uint8_t* smem, Barriers& b,
-                        const AttnParams& p) {
+                        const AttnParams& p, int lane) {
   volatile int* abort = &b.abort;
-  tma_prefetch(qm);
-  tma_prefetch(km);
-  tma_prefetch(vm);
+  if (lane == 0) {
+    tma_prefetch(qm);
+    tma_prefetch(km);
+    tma_prefetch(vm);
+  }
   const int n_slots = p.n_tiles * kTile;
   int q_uses[kSlots][2] = {{0, 0}, {0, 0}};
   int gk = 0, gv = 0;  // K / V tiles issued (ring positions)
   bool ok = true;
+  auto from_lane0 = [&](bool v) {
+    return __shfl_sync(0xffffffffu, v ? 1 : 0, 0) != 0;
+  };
   int it = 0;
   for (int w = blockIdx.x; ok && w < p.n_pairs; w += gridDim.x, ++it) {
     const Pair pr = decode_pair(w, p);
     const int buf = it & 1;
     for (int s = 0; s < kSlots && ok; ++s) {
       if (pr.count[s] == 0) continue;
-      ok = mbar_wait(&b.q_empty[s][buf], (q_uses[s][buf] & 1) ^ 1, abort,
-                     p.status, VEDA_STATUS_TIMEOUT);
+      if (lane == 0) {
+        ok = mbar_wait(&b.q_empty[s][buf], (q_uses[s][buf] & 1) ^ 1, abort,
+                       p.status, VEDA_STATUS_TIMEOUT, p.wait_ns);
+        if (ok) {
+          mbar_expect_tx(&b.q_full[s][buf], kQBytes);
+          tma_load_2d(qm, q_tile(smem, s, buf), &b.q_full[s][buf], 0,
+                      pr.head * n_slots + pr.qt[s] * kTile);
+        }
+      }
+      ok = from_lane0(ok);
       if (!ok) break;
-      mbar_expect_tx(&b.q_full[s][buf], kQBytes);
-      tma_load_2d(qm, q_tile(smem, s, buf), &b.q_full[s][buf], 0,
-                  pr.head * n_slots + pr.qt[s] * kTile);
       ++q_uses[s][buf];
     }
+    const int v_head = p.out_heads != nullptr ? __ldg(p.out_heads + pr.head)
+                                              : pr.head;
     const int steps = max(pr.count[0], pr.count[1]);
     for (int j = 0; j < steps && ok; ++j) {
       for (int s = 0; s < kSlots && ok; ++s) {
         if (j >= pr.count[s]) continue;
         int t = __ldg(pr.idx[s] + j);
-        if (t < 0 || t >= p.n_tiles) report(p.status, VEDA_STATUS_BAD_INDEX);
+        if (lane == 0 && (t < 0 || t >= p.n_tiles))
+          report(p.status, VEDA_STATUS_BAD_INDEX);
         t = clamp_tile(t, p.n_tiles);
         const int stage = gk % kStages;
         const uint32_t ph = (gk / kStages) & 1;
-        ok = mbar_wait(&b.k_empty[stage], ph ^ 1, abort, p.status,
-                       VEDA_STATUS_TIMEOUT);
+        if (lane == 0) {
+          ok = mbar_wait(&b.k_empty[stage], ph ^ 1, abort, p.status,
+                         VEDA_STATUS_TIMEOUT, p.wait_ns);
+          if (ok && !(p.withhold_first_k && blockIdx.x == 0 && gk == 0)) {
+            mbar_expect_tx(&b.k_full[stage], kKBytes);
+            tma_load_2d(km, smem + kSmemK + stage * kKBytes,
+                        &b.k_full[stage], 0, pr.head * n_slots + t * kTile);
+          }
+          if (ok)
+            ok = mbar_wait(&b.v_empty[stage], ph ^ 1, abort, p.status,
+                           VEDA_STATUS_TIMEOUT, p.wait_ns);
+          if (ok) mbar_expect_tx(&b.v_full[stage], kVBytes);
+        }
+        ok = from_lane0(ok);
         if (!ok) break;
-        mbar_expect_tx(&b.k_full[stage], kKBytes);
-        tma_load_2d(km, smem + kSmemK + stage * kKBytes, &b.k_full[stage], 0,
-                    pr.head * n_slots + t * kTile);
         ++gk;
-        ok = mbar_wait(&b.v_empty[stage], ph ^ 1, abort, p.status,
-                       VEDA_STATUS_TIMEOUT);
-        if (!ok) break;
-        mbar_expect_tx(&b.v_full[stage], kVBytes);
         uint8_t* vdst = smem + kSmemV + stage * kVBytes;
-        tma_load_3d(vm, vdst, &b.v_full[stage], 0, pr.head, t * kTile);
-        tma_load_3d(vm, vdst + kVBytes / 2, &b.v_full[stage], 64, pr.head,
-                    t * kTile);
+        if (p.v_perm == nullptr) {
+          if (lane == 0) {
+            tma_load_3d(vm, vdst, &b.v_full[stage], 0, pr.head, t * kTile);
+            tma_load_3d(vm, vdst + kVBytes / 2, &b.v_full[stage], 64,
+                        pr.head, t * kTile);
+          }
+        } else {
+          int y[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int64_t r = __ldg(p.v_perm + static_cast<int64_t>(t) * kTile +
+                                    4 * lane + i);
+            y[i] = (r < 0 || r >= p.seq_len)
+                       ? p.v_rows
+                       : static_cast<int>(r * p.v_heads + v_head);
+          }
+          uint8_t* rows = vdst + 4 * lane * 128;
+          tma_gather4(vm, rows, &b.v_full[stage], 0, y[0], y[1], y[2], y[3]);
+          tma_gather4(vm, rows + kVBytes / 2, &b.v_full[stage], 64, y[0],
+                      y[1], y[2], y[3]);
+        }
         ++gv;
       }
     }
   }
   // Let every copy this CTA started land before it can exit.
-  for (int s = 0; s < kSlots; ++s)
-    for (int buf = 0; buf < 2; ++buf)
-      if (q_uses[s][buf] > 0)
-        drain_wait(&b.q_full[s][buf], (q_uses[s][buf] - 1) & 1, p.status);
-  for (int g = gk - kStages; g < gk; ++g)
-    if (g >= 0) drain_wait(&b.k_full[g % kStages], (g / kStages) & 1, p.status);
-  for (int g = gv - kStages; g < gv; ++g)
-    if (g >= 0) drain_wait(&b.v_full[g % kStages], (g / kStages) & 1, p.status);
+  if (lane == 0) {
+    for (int s = 0; s < kSlots; ++s)
+      for (int buf = 0; buf < 2; ++buf)
+        if (q_uses[s][buf] > 0)
+          drain_wait(&b.q_full[s][buf], (q_uses[s][buf] - 1) & 1, p);
+    for (int g = gk - kStages; g < gk; ++g)
+      if (g >= 0) drain_wait(&b.k_full[g % kStages], (g / kStages) & 1, p);
+    for (int g = gv - kStages; g < gv; ++g)
+      if (g >= 0) drain_wait(&b.v_full[g % kStages], (g / kStages) & 1, p);
+  }
+  __syncwarp();
 }
 
 // Warp 1, one thread: every tcgen05.mma of the CTA, in a fixed interleave
@@ -273,11 +341,11 @@ __device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
   // in order, so their parities are unambiguous).
   auto k_ready = [&]() {
     return mbar_wait(&b.k_full[gk % kStages], (gk / kStages) & 1, abort,
-                     p.status, VEDA_STATUS_TIMEOUT);
+                     p.status, VEDA_STATUS_TIMEOUT, p.wait_ns);
   };
   auto v_ready = [&]() {
     return mbar_wait(&b.v_full[gv % kStages], (gv / kStages) & 1, abort,
-                     p.status, VEDA_STATUS_TIMEOUT);
+                     p.status, VEDA_STATUS_TIMEOUT, p.wait_ns);
   };
   // S[s] = Q[s] K^T of the next K in the ring (landed); frees the K stage,
   // signals S.
@@ -318,7 +386,7 @@ __device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
     for (int s = 0; s < kSlots && ok; ++s) {
       if (pr.count[s] == 0) continue;
       ok = mbar_wait(&b.q_full[s][buf], q_uses[s][buf] & 1, abort, p.status,
-                     VEDA_STATUS_TIMEOUT);
+                     VEDA_STATUS_TIMEOUT, p.wait_ns);
       ++q_uses[s][buf];
       if (ok) ok = k_ready();
       if (ok) qk(s, buf);
@@ -334,13 +402,13 @@ __device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
         if (ok && more) ok = k_ready();
         if (ok)
           ok = mbar_wait(&b.p_full[s], tiles[s] & 1, abort, p.status,
-                         VEDA_STATUS_TIMEOUT);
+                         VEDA_STATUS_TIMEOUT, p.wait_ns);
         ++tiles[s];
         // the first P V of a walk overwrites O: the last walk's rows must
         // have been read out of it
         if (ok && j == 0 && items[s] > 0)
           ok = mbar_wait(&b.o_free[s], (items[s] - 1) & 1, abort, p.status,
-                         VEDA_STATUS_TIMEOUT);
+                         VEDA_STATUS_TIMEOUT, p.wait_ns);
         if (!ok) break;
         pv(s, j > 0);
         if (more) {
@@ -355,7 +423,7 @@ __device__ void issue_mma(uint8_t* smem, Barriers& b, uint32_t tmem,
   }
   // Every MMA this CTA issued completes before TMEM is released.
   tc_commit(&b.fin);
-  drain_wait(&b.fin, 0, p.status);
+  drain_wait(&b.fin, 0, p);
 }
 
 // 16 bytes to every GPU bound to the multicast object behind `mc` (one
@@ -450,13 +518,14 @@ constexpr uint32_t kMaskBits = 0xFF800000u - kMagicBits;
 // Waits (bounded) until more than `walks` walks are published.
 __device__ __forceinline__ bool wait_published(const int* counter, int walks,
                                                volatile int* abort,
-                                               int32_t* status) {
+                                               int32_t* status,
+                                               uint64_t wait_ns) {
   const volatile int* n = counter;
   if (*n <= walks) {
     const uint64_t start = global_ns();
     while (*n <= walks) {
       if (*abort) return false;
-      if (global_ns() - start > kWaitLimitNs) {
+      if (global_ns() - start > wait_ns) {
         *abort = 1;
         report(status, VEDA_STATUS_TIMEOUT);
         return false;
@@ -498,7 +567,8 @@ __device__ void push_slot(int s, Barriers& b, const AttnParams& p, int lane) {
     const int qt = pr.qt[s];
     if (qt >= p.n_tiles) continue;
     for (int q = 0; q < 4 && ok; ++q) {
-      ok = wait_published(&b.published[s][q], walks, abort, p.status);
+      ok = wait_published(&b.published[s][q], walks, abort, p.status,
+                            p.wait_ns);
       if (!ok) break;
       // 32 rows x 256 bytes: lane l moves bytes 16 (l % 16) of rows
       // l / 16, l / 16 + 2, ..., four loads in flight.
@@ -617,7 +687,7 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
       cur.valid = valid_cur;
 
       good = mbar_wait(&b.s_full[slot], tiles & 1, abort, p.status,
-                       VEDA_STATUS_TIMEOUT);
+                       VEDA_STATUS_TIMEOUT, p.wait_ns);
       ++tiles;
       if (!__all_sync(0xffffffffu, good)) {
         good = false;
@@ -722,7 +792,7 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
     }
     if (!good) break;
     good = mbar_wait(&b.o_ready[slot], items & 1, abort, p.status,
-                     VEDA_STATUS_TIMEOUT);
+                     VEDA_STATUS_TIMEOUT, p.wait_ns);
     ++items;
     if (!__all_sync(0xffffffffu, good)) {
       good = false;
@@ -816,8 +886,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp < 4) {
     regs_dec<kLowRegs>();
     if (run && warp == 0) {
-      if (lane == 0) produce(&q_map, &k_map, &v_map, smem, b, p);
-      __syncwarp();
+      produce(&q_map, &k_map, &v_map, smem, b, p, lane);
     } else if (run && warp == 1) {
       if (lane == 0) issue_mma<VT>(smem, b, tmem, p);
       __syncwarp();
@@ -880,7 +949,8 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
            int heads, int n_tiles, void* out, void* out_mc,
            int64_t out_stride_n, int64_t out_stride_h, int32_t* status,
            void* stream, const int64_t* perm = nullptr, int64_t seq_len = 0,
-           const int32_t* out_heads = nullptr) {
+           const int32_t* out_heads = nullptr,
+           uint64_t wait_ns = kWaitLimitNs, int withhold_first_k = 0) {
   if (int rc = check_device()) return rc;
   if (perm != nullptr && (seq_len <= 0 || out_mc != nullptr))
     return fail(VEDA_ERR_INVALID,
@@ -915,18 +985,35 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
                               CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
-  {
+  const CUtensorMapDataType v_type = v_dtype == VEDA_BF16
+                                         ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  int v_heads = 0;
+  if (perm == nullptr) {  // V in tile order: [slot][head][dim], 64 x 128 boxes
     const uint64_t dims[3] = {static_cast<uint64_t>(kDim),
                               static_cast<uint64_t>(heads),
                               static_cast<uint64_t>(n_slots)};
     const uint64_t strides[2] = {static_cast<uint64_t>(v_stride_h) * 2,
                                  static_cast<uint64_t>(v_stride_n) * 2};
     const uint32_t box[3] = {64, 1, kTile};
-    if (int rc = encode_tiled(
-            &vm,
-            v_dtype == VEDA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-            3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (int rc = encode_tiled(&vm, v_type, 3, v, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  } else {  // packed V: rows (s, h) of a [seq_len * v_heads, 128] view
+    if (v_stride_h <= 0 || v_stride_n % v_stride_h != 0)
+      return fail(VEDA_ERR_INVALID,
+                  "packed v needs evenly spaced rows (stride_n a multiple of "
+                  "stride_h); make it contiguous");
+    v_heads = static_cast<int>(v_stride_n / v_stride_h);
+    if (v_heads < heads || seq_len * v_heads >= (1ll << 31) - 1)
+      return fail(VEDA_ERR_INVALID, "packed v: %lld rows x %d heads",
+                  static_cast<long long>(seq_len), v_heads);
+    const uint64_t dims[2] = {static_cast<uint64_t>(kDim),
+                              static_cast<uint64_t>(seq_len) * v_heads};
+    const uint64_t strides[1] = {static_cast<uint64_t>(v_stride_h) * 2};
+    const uint32_t box[2] = {64, 1};
+    if (int rc = encode_tiled(&vm, v_type, 2, v, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
   // The output as [slot][head][dim], written by TMA in 32 x 32 boxes.
@@ -960,6 +1047,11 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
   p.perm = perm;
   p.seq_len = seq_len;
   p.out_heads = out_heads;
+  p.v_perm = perm;
+  p.v_heads = v_heads;
+  p.v_rows = static_cast<int>(seq_len * v_heads);
+  p.wait_ns = wait_ns;
+  p.withhold_first_k = withhold_first_k;
   p.n_tiles = n_tiles;
   p.width = width;
   p.heads = heads;
@@ -1014,4 +1106,20 @@ extern "C" int veda_sparse_attention_packed(
                 v_stride_h, index, width, count, valid_count, heads, n_tiles,
                 out, nullptr, out_stride_n, out_stride_h, status, stream, perm,
                 seq_len, out_heads);
+}
+
+extern "C" int veda_debug_sparse_attention(
+    const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
+    const float* k_scale, const void* v, int v_dtype, int64_t v_stride_n,
+    int64_t v_stride_h, const int32_t* index, int width, const int32_t* count,
+    const int32_t* valid_count, int heads, int n_tiles, void* out,
+    int64_t out_stride_n, int64_t out_stride_h, uint64_t wait_ns,
+    int withhold_first_k_load, int32_t* status, void* stream) {
+  if (wait_ns == 0 || wait_ns > kWaitLimitNs)
+    return fail(VEDA_ERR_INVALID, "wait_ns must be in (0, %llu]",
+                static_cast<unsigned long long>(kWaitLimitNs));
+  return attend(q_i8, q_scale, k_i8, k_scale, v, v_dtype, v_stride_n,
+                v_stride_h, index, width, count, valid_count, heads, n_tiles,
+                out, nullptr, out_stride_n, out_stride_h, status, stream,
+                nullptr, 0, nullptr, wait_ns, withhold_first_k_load ? 1 : 0);
 }

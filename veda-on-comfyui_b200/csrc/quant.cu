@@ -80,9 +80,12 @@ __device__ __forceinline__ int8_t quant_one(float x, float b, float y) {
 
 // The tile is held as raw 16-bit words (32 registers a thread) and widened
 // twice, once for the block max and once for the codes, so three CTAs fit
-// on an SM and more loads are in flight. POOL adds the TripPool features.
+// on an SM and more loads are in flight. POOL adds the TripPool features;
+// their accumulators would leave room for two CTAs only, so the pooling
+// variant reads its tile a second time for the codes (an L2 hit: the tile
+// was read microseconds earlier by the same CTA) and keeps three.
 template <typename T, bool POOL>
-__global__ void __launch_bounds__(kQuantThreads, POOL ? 2 : 3)
+__global__ void __launch_bounds__(kQuantThreads, 3)
     quant_pool_kernel(const QuantParams p) {
   __shared__ float amax_sh[8][2];
   __shared__ float pool_sh[POOL ? 8 : 1][3][kDim];
@@ -203,6 +206,13 @@ __global__ void __launch_bounds__(kQuantThreads, POOL ? 2 : 3)
   for (int i = 0; i < 8; ++i) {
     const float b = sc[i >> 2], y = inv[i >> 2];
     float f[8];
+    if (POOL) {
+      int64_t row = static_cast<int64_t>(tile) * kTile + rg + 16 * i;
+      if (p.perm != nullptr) row = __ldg(p.perm + row);
+      raw[i] = row >= 0 && (p.perm == nullptr || row < p.seq_len)
+                   ? __ldg(reinterpret_cast<const uint4*>(x + row * p.stride_n))
+                   : make_uint4(0, 0, 0, 0);
+    }
     unpack8(raw[i], f, T());
     uint32_t lo = 0, hi = 0;
 #pragma unroll

@@ -56,6 +56,7 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _L = ctypes.c_int64
 _F = ctypes.c_float
+_U64 = ctypes.c_uint64
 
 # name -> argument types, in the order of include/veda_b200.h
 SIGNATURES = {
@@ -82,6 +83,9 @@ SIGNATURES = {
     'veda_sparse_attention_packed': [_P, _P, _P, _P, _P, _I, _L, _L, _P, _I,
                                      _P, _P, _I, _I, _P, _L, _L, _P, _L, _P,
                                      _P, _P],
+    'veda_debug_sparse_attention': [_P, _P, _P, _P, _P, _I, _L, _L, _P, _I,
+                                    _P, _P, _I, _I, _P, _L, _L, _U64, _I, _P,
+                                    _P],
     'veda_gather_tiles': [_P, _I, _L, _L, _I, _I, _P, _I, _P, _I, _P, _P],
     'veda_scatter_tiles': [_P, _I, _P, _I, _P, _I, _I, _P, _L, _L, _I, _P],
 }

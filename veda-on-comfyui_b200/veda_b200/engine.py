@@ -4,14 +4,14 @@ The reference engine (core/engine.py:246-326) runs, per head group and head
 chunk, about sixty torch launches: gather q/k/v into tile order, pool, bmm
 logits, top-k, dense block mask, a host-synchronising index list, quantise
 Q, quantise K, cast V, attend, scatter. This fast path does the same call
-in five kernels with no host synchronisation:
+in four kernels with no host synchronisation:
 
-    [gather V] -> quant_pool (Q, K int8 + TripPool features, one read; packed
-                  rows are read through the tile permutation)
-               -> tile_logits (predictor; skipped when scores are given)
-               -> select (top-k straight into ascending index lists)
-               -> sparse_attention (tcgen05; a packed output is written
-                  through the permutation)
+    quant_pool (Q, K int8 + TripPool features, one read; packed rows are
+                read through the tile permutation)
+    -> tile_logits (predictor; skipped when scores are given)
+    -> select (top-k straight into ascending index lists)
+    -> sparse_attention (tcgen05; packed V is read and the output written
+                         through the permutation)
 
 `full=True` is a full-attention layer or step (full_attention_layers /
 full_attention_steps, 0% sparsity): the same attention kernel over every
@@ -143,13 +143,12 @@ class VedaAttention:
             self._dense[key] = hit
         return hit[1], hit[2]
 
-    def _ids(self, heads, n_heads: int, device) -> tuple:
+    def _ids(self, heads, n_heads: int, device) -> torch.Tensor:
         key = (tuple(int(h) for h in heads), n_heads, device)
         hit = self._head_ids.get(key)
         if hit is None:
             ids = ops.head_ids(list(key[0]), n_heads, device)
-            hit = (ids, ids.to(torch.int64))
-            self._head_ids[key] = hit
+            self._head_ids[key] = hit = ids
         return hit
 
     @torch.no_grad()
@@ -161,11 +160,11 @@ class VedaAttention:
         [S, H, 128] out in v's dtype.
 
         Each group runs its own kernel sequence on the same packed tensors:
-        V of its heads gathered into its tile order, Q and K quantised (and
-        pooled) through its permutation and head ids, its scores selected
-        into lists, and its attention written through the permutation to its
-        heads of `out`. No per-group copy of q, k or v is made, nothing
-        synchronises the host, and the selection counts feed `self.stats`.
+        Q and K quantised (and pooled) through its permutation and head ids,
+        its scores selected into lists, and its attention reading V and
+        writing its heads of `out` through the permutation. No per-group
+        copy of q, k or v is made, nothing synchronises the host, and the
+        selection counts feed `self.stats`.
         """
         seq_len, n_heads, dim = q.shape
         device = q.device
@@ -181,12 +180,11 @@ class VedaAttention:
             if layout.seq_len != seq_len:
                 raise ValueError(f'a layout of {layout.seq_len} rows for a '
                                  f'sequence of {seq_len}')
-            ids32, ids64 = self._ids(group.heads, n_heads, device)
+            ids32 = self._ids(group.heads, n_heads, device)
             perm = layout.perm
             need_pool = not full and group.scores is None
             if need_pool and group.projections is None:
                 raise ValueError('a head group needs scores or projections')
-            v_t = ops.gather_tiles(v, perm, ids64)
             quant = ops.quant_pool(
                 q, k, layout.valid_count, layout.n_video_tiles,
                 scale * kernels.LOG2E, pool=need_pool,
@@ -203,7 +201,7 @@ class VedaAttention:
                 index, count = self.select(scores, layout)
                 self.stats.add_lists(count, layout)
             ops.sparse_attention(quant['q_i8'], quant['q_scale'],
-                                 quant['k_i8'], quant['k_scale'], v_t, index,
+                                 quant['k_i8'], quant['k_scale'], v, index,
                                  count, layout.valid_count, out=out,
                                  perm=perm, heads=ids32)
         return out
@@ -267,12 +265,10 @@ class VedaAttention:
             q_t, k_t, v_t = q, k, v
         else:
             # Packed rows: the quantisation reads Q and K through the
-            # permutation and the attention epilogue writes the output
-            # through it, so only V is gathered into tile order.
+            # permutation, the attention reads V and writes the output
+            # through it, so nothing is gathered into tile order.
             perm = layout.perm
-            q_t, k_t = q, k
-            v_t = ops.gather_tiles(v, perm,
-                                   torch.arange(heads, device=q.device))
+            q_t, k_t, v_t = q, k, v
         dim = q.shape[-1]
         scale = dim ** -0.5 if self.softmax_scale is None \
             else self.softmax_scale

@@ -279,43 +279,56 @@ def sparse_attention(q_i8, q_scale, k_i8, k_scale, v, index, count,
                      out_multicast: int = 0,
                      perm: torch.Tensor | None = None,
                      heads: torch.Tensor | None = None):
-    """INT8 block-sparse attention. v [N, H, 128] 16-bit; returns out
-    [N, H, 128] of v's dtype (or writes `out`, any row / head strides).
+    """INT8 block-sparse attention. v [N, H, 128] 16-bit in tile order;
+    returns out [N, H, 128] of v's dtype (or writes `out`, any row / head
+    strides).
 
     out_multicast: the NVSwitch multicast address of `out`'s first element
     (head sharding): rows are stored through it to every GPU bound to the
     multicast object, instead of to `out` alone.
-    perm: packed output. `out` ([S, H, 128], required) receives row `slot`
-    of the result at row perm[slot]; padding slots (perm < 0) are dropped:
-    the scatter back to sequence order happens in the kernel's epilogue.
-    heads: with `perm`, one head group: head h of v / the lists is written to
-    head heads[h] of `out` ([H'] int32 device ids, see `head_ids`).
+    perm: packed rows. v is then [S, H, 128] in sequence order and slot i of
+    the tile order reads its row perm[i] (< 0: padding, zeros); `out`
+    ([S, H, 128], required) receives row `slot` of the result at row
+    perm[slot], padding slots dropped. Neither the gather of V nor the
+    scatter of the output is a pass of its own.
+    heads: with `perm`, one head group: list head h reads head heads[h] of v
+    and writes head heads[h] of `out` ([H'] int32 device ids, see
+    `head_ids`).
     """
     _check_rows(v, 'v')
     device = require_device(q_i8, k_i8, v, index, count, valid_count)
     head_map = heads
-    n, heads, _ = v.shape
+    if head_map is not None and perm is None:
+        raise ValueError('a head group needs packed rows (perm)')
+    if perm is None:
+        n, heads, _ = v.shape
+    else:
+        if out is None or out_multicast:
+            raise ValueError('packed rows need `out` and no multicast')
+        perm = perm.to(device=device, dtype=torch.int64).contiguous()
+        n = perm.numel()
+        heads = v.shape[1] if head_map is None else head_map.numel()
+        if head_map is not None and (head_map.dtype != torch.int32 or
+                                     head_map.device != device):
+            raise ValueError('heads must be int32 ids on the device')
+        if v.shape[0] != out.shape[0]:
+            raise ValueError(f'packed v has {v.shape[0]} rows, out '
+                             f'{out.shape[0]}')
+        if head_map is None and out.shape[1] != v.shape[1]:
+            raise ValueError('out must have v\'s heads')
+        if v.stride(0) % v.stride(1) != 0 or \
+                v.stride(0) // v.stride(1) < v.shape[1]:
+            # the kernel reads packed V as evenly spaced [S * H', 128] rows
+            v = v.contiguous()
     n_tiles = n // TILE
-    if perm is not None and (out is None or out_multicast):
-        raise ValueError('a packed output needs `out` and no multicast')
+    if index.shape[0] != heads or count.shape[0] != heads:
+        raise ValueError(f'lists for {index.shape[0]} heads, attention over '
+                         f'{heads}')
     if out is None:
         out = torch.empty(n, heads, HEAD_DIM, dtype=v.dtype, device=device)
     _check_rows(out, 'out')
     if out.dtype != v.dtype:
         raise ValueError('out must have v\'s dtype')
-    if head_map is not None and perm is None:
-        raise ValueError('a head group needs a packed output (perm)')
-    if perm is not None:
-        perm = perm.to(device=device, dtype=torch.int64).contiguous()
-        if head_map is not None:
-            if head_map.dtype != torch.int32 or head_map.device != device or \
-                    head_map.numel() != v.shape[1]:
-                raise ValueError('heads must be int32 ids on the device, one '
-                                 'per head of v')
-        elif out.shape[1] != v.shape[1]:
-            raise ValueError('out must have v\'s heads')
-        if perm.numel() != n:
-            raise ValueError('perm must have a slot per row of v')
     index = index.to(torch.int32).contiguous()
     count = count.to(torch.int32).contiguous()
     valid = valid_count.to(torch.int32).contiguous()
