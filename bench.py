@@ -419,6 +419,72 @@ def predictor_path(sets: list, device, steps: int, hbm_gbs: float) -> dict:
     return out
 
 
+def packed_call(device, steps: int) -> dict:
+    """A ComfyUI-shaped call on packed rows, timed against the same call on
+    rows already in tile order: one layer of an 8 x 48 x 84 video span
+    (32,256 tokens, tiles 1 x 8 x 16, 288 tiles with padding slots in W),
+    H=24, 90% sparse, through `VedaAttention.layer`. On packed rows the
+    quantisation reads Q and K and the attention reads V and writes the
+    output through the tile permutation; the tile-order call runs the same
+    kernels on pre-gathered rows with the same lists. Two input sets of
+    594 MB alternate (> L2); CUDA events, median of `steps` calls each."""
+    from veda_b200 import engine, ops, selection, tiling
+    span = tiling.TiledSpan(0, (8, 48, 84), tiling.TileShape(1, 8, 16))
+    seq = 8 * 48 * 84
+    layout = tiling.build_tile_layout([span], seq, device)
+    eng = engine.VedaAttention(selection.Budget.sparsity(90))
+    heads = torch.arange(HEADS, device=device)
+    g = torch.Generator(device=device).manual_seed(4242)
+    sets = []
+    for _ in range(2):
+        q, k, v = (torch.randn(seq, HEADS, DIM, generator=g, device=device,
+                               dtype=torch.bfloat16) for _ in range(3))
+        n = layout.n_video_tiles
+        scores = torch.rand(HEADS, n, n, generator=g, device=device)
+        tiled = tuple(ops.gather_tiles(x, layout.perm, heads)
+                      for x in (q, k, v))
+        sets.append(((q, k, v), tiled, scores))
+    out_packed = torch.empty(seq, HEADS, DIM, dtype=torch.bfloat16,
+                             device=device)
+    out_tiled = torch.empty(layout.num_slots, HEADS, DIM,
+                            dtype=torch.bfloat16, device=device)
+
+    def run(kind: str) -> float:
+        times = []
+        for i in range(steps + 3):
+            packed, tiled, scores = sets[i % 2]
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            if kind == 'packed':
+                eng.layer(*packed, layout, scores=scores, out=out_packed,
+                          tiled=False)
+            else:
+                eng.layer(*tiled, layout, scores=scores, out=out_tiled,
+                          tiled=True)
+            e1.record()
+            if i >= 3:
+                times.append((e0, e1))
+        torch.cuda.synchronize(device)
+        return statistics.median(a.elapsed_time(b) for a, b in times)
+
+    packed_ms, tiled_ms = run('packed'), run('tiled')
+    same = True
+    for packed, tiled, scores in sets:
+        eng.layer(*packed, layout, scores=scores, out=out_packed,
+                  tiled=False)
+        eng.layer(*tiled, layout, scores=scores, out=out_tiled, tiled=True)
+        back = torch.empty_like(out_packed)
+        ops.scatter_tiles_(back, out_tiled, layout.perm, heads)
+        same = same and bool(torch.equal(back, out_packed))
+    ops.check_status(device)
+    return {'workload': '8 x 48 x 84 video span (32,256 tokens), tiles '
+                        '1 x 8 x 16 (288 tiles, padding in W), H=24, 90% '
+                        'sparse, one layer through VedaAttention.layer',
+            'packed_ms': packed_ms, 'tile_order_ms': tiled_ms,
+            'packed_over_tile_order': packed_ms / tiled_ms,
+            'bit_equal_after_scatter': same, 'steps': steps}
+
+
 def _reference_cpu_modules():
     """(reference, selection, tiling) of the reference's torch core from the
     unmodified package in baseline/_ref, or None when it is absent."""
@@ -1017,6 +1083,7 @@ def main():
         if world == 1:
             line['predictor_path'] = predictor_path(
                 sets[:2], device, max(args.steps, 10), peaks['hbm_gbs'])
+            line['packed_call'] = packed_call(device, max(args.steps, 10))
         if world == 1 and not args.no_cpu_baseline:
             line['cpu_baseline'] = cpu_reference()
         print(json.dumps(line), file=json_out, flush=True)

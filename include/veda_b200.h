@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define VEDA_ABI_VERSION 3
+#define VEDA_ABI_VERSION 4
 
 /* Return codes. */
 #define VEDA_OK 0
@@ -242,35 +242,34 @@ int veda_sparse_attention_multicast(
  * strides and that every perm entry is below seq_len: rows at or past
  * seq_len are treated as padding, but seq_len itself is not checked
  * against the tensors (raw pointers carry no extent).
+ *   v, v_tiled   optional (both NULL or neither): packed V [seq_len, *,
+ *                128] of q's dtype at v_stride_n / v_stride_h, copied
+ *                through the same permutation and head ids into v_tiled
+ *                [n_slots, heads, 128] (tile order, contiguous), the V
+ *                operand of veda_sparse_attention_packed. Same bits as
+ *                veda_gather_tiles of V, in the same launch as Q and K.
  *   head_ids     [heads] int32, or NULL for heads 0 .. heads - 1: output
  *                head h is input head head_ids[h], so one head group of a
  *                layer (core/plans.py:25-29 HeadGroup; core/engine.py:
  *                282-297) is quantised without a copy of q[:, group]. The
- *                caller guarantees every id is a head of q and k.
+ *                caller guarantees every id is a head of q, k and v.
  */
 int veda_quant_pool_packed(
     const void* q, const void* k, int dtype, int64_t stride_n,
     int64_t stride_h, int64_t seq_len, const int64_t* perm, int n_slots,
     int heads, const int32_t* valid_count, int n_video_tiles,
     float q_pre_scale, int8_t* q_i8, float* q_scale, int8_t* k_i8,
-    float* k_scale, float* feats_q, float* feats_k, const int32_t* head_ids,
-    void* stream);
+    float* k_scale, float* feats_q, float* feats_k, const void* v,
+    int64_t v_stride_n, int64_t v_stride_h, void* v_tiled,
+    const int32_t* head_ids, void* stream);
 
 /*
- * veda_sparse_attention on packed rows: V is read and the output written
- * in sequence order through the tile permutation, so neither the gather of
- * V (core/tiling.py:227-242) nor the scatter of the output (:245-252,
- * scatter_tiles_) is a pass of its own.
- *   v            [seq_len, heads_total, 128] 16-bit with evenly spaced rows
- *                (v_stride_n a multiple of v_stride_h; heads_total =
- *                v_stride_n / v_stride_h); slot i of the tile order reads
- *                row perm[i] (padding slots, perm < 0, read zeros), head
- *                out_heads[h] (or h).
- *   out          row `slot` of the result goes to row perm[slot] of `out`
- *                ([seq_len, heads, 128], any row and head strides); padding
- *                slots are dropped.
- * Same bits as veda_gather_tiles of V, veda_sparse_attention and
- * veda_scatter_tiles.
+ * veda_sparse_attention with a packed output: row `slot` of the result goes
+ * to row perm[slot] of `out` ([seq_len, heads, 128], any row and head
+ * strides), padding slots (perm < 0) are dropped, so the scatter of
+ * core/tiling.py:245-252 (scatter_tiles_) happens in the kernel's epilogue.
+ * V is in tile order (the v_tiled output of veda_quant_pool_packed).
+ * Same bits as veda_sparse_attention followed by veda_scatter_tiles.
  * The caller guarantees that `out` holds seq_len rows at the given strides;
  * slots whose perm entry is at or past seq_len are dropped like padding.
  *   out_heads    [heads] int32, or NULL for heads 0 .. heads - 1: head h of

@@ -1,9 +1,9 @@
 """The packed-row paths against the separate passes they fold in, on a
 layout whose permutation is not the identity (spans, padding slots):
-quantisation reading packed rows through the permutation equals
-gather_tiles then quantisation, and the attention reading V and writing
-its output through the permutation equals gather_tiles, the attention and
-scatter_tiles_, bit for bit."""
+quantisation reading packed rows through the permutation, with V copied
+into tile order by the same launch, equals gather_tiles then quantisation;
+the attention epilogue writing through the permutation equals the
+attention then scatter_tiles_; bit for bit."""
 
 import pytest
 import torch
@@ -26,61 +26,25 @@ def test_packed_quantisation_equals_gather_then_quantisation(cuda_device,
     case = problems.CASES['gpu_problem']
     layout = helpers.device_layout(case, cuda_device)
     assert not layout.identity
-    q, k, _ = _packed(case, dtype, cuda_device)
+    q, k, v = _packed(case, dtype, cuda_device)
     heads = torch.arange(q.shape[1], device=cuda_device)
     pre = 128 ** -0.5 * kernels.LOG2E
     want = ops.quant_pool(ops.gather_tiles(q, layout.perm, heads),
                           ops.gather_tiles(k, layout.perm, heads),
                           layout.valid_count, layout.n_video_tiles, pre)
     got = ops.quant_pool(q, k, layout.valid_count, layout.n_video_tiles, pre,
-                         perm=layout.perm)
+                         perm=layout.perm, v=v)
     for key in ('q_i8', 'q_scale', 'k_i8', 'k_scale', 'feats_q', 'feats_k'):
         assert torch.equal(got[key], want[key]), key
-
-
-def _lists_and_quant(case, layout, q, k, device):
-    from veda_b200 import kernels, ops
-    from veda_b200 import selection as vs
-    scores = problems.make_scores(case)
-    index, count = vs.select_index(torch.from_numpy(scores).to(device),
-                                   layout, helpers.product_blocks(case, layout))
-    quant = ops.quant_pool(q, k, layout.valid_count, 0,
-                           128 ** -0.5 * kernels.LOG2E, pool=False,
-                           perm=layout.perm)
-    return (quant['q_i8'], quant['q_scale'], quant['k_i8'],
-            quant['k_scale']), index, count
-
-
-@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
-def test_packed_attention_equals_gather_attention_scatter(cuda_device, dtype):
-    """V read through the permutation and the output written through it:
-    the same bits as gather_tiles(V), the tile-order attention and
-    scatter_tiles_."""
-    from veda_b200 import ops
-    case = problems.CASES['gpu_problem']
-    layout = helpers.device_layout(case, cuda_device)
-    q, k, v = _packed(case, dtype, cuda_device)
-    quant, index, count = _lists_and_quant(case, layout, q, k, cuda_device)
-    heads = torch.arange(v.shape[1], device=cuda_device)
-    tiled = ops.sparse_attention(*quant, ops.gather_tiles(v, layout.perm,
-                                                          heads),
-                                 index, count, layout.valid_count)
-    want = torch.zeros(case.seq_len, v.shape[1], 128, dtype=dtype,
-                       device=cuda_device)
-    ops.scatter_tiles_(want, tiled, layout.perm, heads)
-    got = torch.zeros_like(want)
-    ops.sparse_attention(*quant, v, index, count, layout.valid_count,
-                         out=got, perm=layout.perm)
-    ops.check_status(cuda_device)
-    assert torch.equal(got, want)
+    assert torch.equal(got['v_tiled'], ops.gather_tiles(v, layout.perm,
+                                                        heads))
 
 
 @pytest.mark.parametrize('view', ['fused_qkv', 'head_major'])
-def test_packed_attention_head_group_on_strided_v(cuda_device, view):
-    """A head group over V viewed out of a fused [S, 3H, 128] projection
-    (rows evenly spaced, read in place) or out of a head-major [H, S, 128]
-    buffer (copied once to packed rows), against gather / attend /
-    scatter of the same heads."""
+def test_packed_v_copy_of_a_head_group_on_strided_v(cuda_device, view):
+    """A head group's V copied into tile order from V viewed out of a fused
+    [S, 3H, 128] projection or out of a head-major [H, S, 128] buffer,
+    against gather_tiles of the same heads."""
     from veda_b200 import ops
     case = problems.CASES['gpu_problem']
     layout = helpers.device_layout(case, cuda_device)
@@ -89,27 +53,37 @@ def test_packed_attention_head_group_on_strided_v(cuda_device, view):
     group = [n_heads - 1, 0] if n_heads > 1 else [0]
     ids32 = ops.head_ids(group, n_heads, cuda_device)
     if view == 'fused_qkv':
-        fused = torch.cat([q, k, v], dim=1)
-        v_view = fused[:, 2 * n_heads:]
+        v_view = torch.cat([q, k, v], dim=1)[:, 2 * n_heads:]
     else:
         v_view = v.transpose(0, 1).contiguous().transpose(0, 1)
-    assert torch.equal(v_view, v)
-    quant = ops.quant_pool(q, k, layout.valid_count, 0, 0.1, pool=False,
-                           perm=layout.perm, heads=ids32)
-    quant = (quant['q_i8'], quant['q_scale'], quant['k_i8'], quant['k_scale'])
-    scores = problems.make_scores(case)
+    assert torch.equal(v_view, v) and not v_view.is_contiguous()
+    got = ops.quant_pool(q, k, layout.valid_count, 0, 0.1, pool=False,
+                         perm=layout.perm, heads=ids32, v=v_view)
+    ops.check_status(cuda_device)
+    assert torch.equal(got['v_tiled'],
+                       ops.gather_tiles(v, layout.perm, ids32.to(torch.int64)))
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
+def test_packed_output_equals_attention_then_scatter(cuda_device, dtype):
+    from veda_b200 import kernels, ops
     from veda_b200 import selection as vs
-    index, count = vs.select_index(
-        torch.from_numpy(scores).to(cuda_device)[group], layout,
-        helpers.product_blocks(case, layout))
-    ids64 = ids32.to(torch.int64)
-    tiled = ops.sparse_attention(*quant, ops.gather_tiles(v, layout.perm,
-                                                          ids64),
-                                 index, count, layout.valid_count)
-    want = torch.zeros_like(v)
-    ops.scatter_tiles_(want, tiled, layout.perm, ids64)
-    got = torch.zeros_like(v)
-    ops.sparse_attention(*quant, v_view, index, count, layout.valid_count,
-                         out=got, perm=layout.perm, heads=ids32)
+    case = problems.CASES['gpu_problem']
+    layout = helpers.device_layout(case, cuda_device)
+    q, k, v, scores, _ = problems.make_problem(case)
+    q, k, v = (t.to(dtype).to(cuda_device) for t in (q, k, v))
+    index, count = vs.select_index(torch.from_numpy(scores).to(cuda_device),
+                                   layout, helpers.product_blocks(case, layout))
+    quant = ops.quant_pool(q, k, layout.valid_count, 0,
+                           128 ** -0.5 * kernels.LOG2E, pool=False)
+    args = (quant['q_i8'], quant['q_scale'], quant['k_i8'], quant['k_scale'],
+            v, index, count, layout.valid_count)
+    tiled = ops.sparse_attention(*args)
+    heads = torch.arange(v.shape[1], device=cuda_device)
+    want = torch.zeros(case.seq_len, v.shape[1], 128, dtype=dtype,
+                       device=cuda_device)
+    ops.scatter_tiles_(want, tiled, layout.perm, heads)
+    got = torch.zeros_like(want)
+    ops.sparse_attention(*args, out=got, perm=layout.perm)
     ops.check_status(cuda_device)
     assert torch.equal(got, want)

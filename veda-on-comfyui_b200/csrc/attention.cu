@@ -109,11 +109,6 @@ struct AttnParams {
   // Packed output of one head group (null: all heads): head h of this call
   // is head out_heads[h] of `out`.
   const int32_t* out_heads;
-  // Packed V (null: V in tile order): V rows are read through this same
-  // permutation from a [seq_len * v_heads, 128] view of [seq_len, v_heads,
-  // 128]; v_rows = seq_len * v_heads is the out-of-range row of padding.
-  const int64_t* v_perm;
-  int v_heads, v_rows;
   int n_tiles, width, heads;
   int n_pairs;           // heads * ceil(n_tiles / 2)
   uint64_t wait_ns;      // bound of every wait (kWaitLimitNs in production)
@@ -198,28 +193,18 @@ __device__ __forceinline__ uint8_t* q_tile(uint8_t* smem, int slot, int buf) {
   return smem + kSmemQ + (2 * slot + buf) * kQBytes;
 }
 
-// TMA gather of four rows (row coordinates y0..y3 of a 2D map with a box one
-// row high) into consecutive 128-byte rows at `dst`; the 128-byte swizzle
-// depends on the shared-memory address only, so the rows land exactly as a
-// tiled load of the same rows in order would put them.
-__device__ __forceinline__ void tma_gather4(const CUtensorMap* map, void* dst,
-                                            uint64_t* bar, int x, int y0,
-                                            int y1, int y2, int y3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4."
-      "mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)),
-      "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
-      : "memory");
-}
-
 // Warp 0: Q tiles per pair, then K / V tiles in the order the MMA thread
 // consumes them (A and B interleaved, tile by tile). Lane 0 waits for the
-// ring stages and issues the Q, K and tile-order V loads. A packed V (one
-// head group of [seq_len, heads, 128] rows, read through the tile
-// permutation) is gathered by the whole warp: lane l brings rows 4 l .. 4 l
-// + 3 of the tile, both 64-column halves, and padding slots read an
-// out-of-range row, which the TMA fills with zeros.
+// ring stages and issues the loads; the warp walks the lists with it so the
+// outcome of each wait is shared by shuffle.
+//
+// V is read in tile order, two 64 x 128-row boxes per tile. Reading packed
+// V through the permutation here was measured and rejected: the TMA engine
+// spends about 65-90 SM clocks per instruction plus about 2.7 clocks per
+// 128-byte row, so a 32 KB tile costs ~680 clocks as two tiled boxes but
+// ~4,300 as 64 four-row gathers (tile::gather4) and ~1,400 even as 16-row
+// boxes, against ~1,100 clocks of attention per tile on a CTA. Packed V is
+// copied into tile order by the quantisation pass instead.
 __device__ void produce(const CUtensorMap* qm, const CUtensorMap* km,
                         const CUtensorMap* vm, uint8_t* smem, Barriers& b,
                         const AttnParams& p, int lane) {
@@ -255,58 +240,58 @@ __device__ void produce(const CUtensorMap* qm, const CUtensorMap* km,
       if (!ok) break;
       ++q_uses[s][buf];
     }
-    const int v_head = p.out_heads != nullptr ? __ldg(p.out_heads + pr.head)
-                                              : pr.head;
+    // Steps (j, s) in issue order: j ascending, both slots per j, a slot
+    // skipped once its list is done. The tile id of the next step is loaded
+    // one step ahead, so its global load overlaps the waits of the step
+    // before instead of following the stage's release.
     const int steps = max(pr.count[0], pr.count[1]);
-    for (int j = 0; j < steps && ok; ++j) {
-      for (int s = 0; s < kSlots && ok; ++s) {
-        if (j >= pr.count[s]) continue;
-        int t = __ldg(pr.idx[s] + j);
-        if (lane == 0 && (t < 0 || t >= p.n_tiles))
-          report(p.status, VEDA_STATUS_BAD_INDEX);
-        t = clamp_tile(t, p.n_tiles);
-        const int stage = gk % kStages;
-        const uint32_t ph = (gk / kStages) & 1;
-        if (lane == 0) {
-          ok = mbar_wait(&b.k_empty[stage], ph ^ 1, abort, p.status,
+    int j = 0, s = 0;
+    // slot-indexed fields by select, so the pair stays in registers
+    auto count_of = [&](int ss) { return ss == 0 ? pr.count[0] : pr.count[1]; };
+    auto list_of = [&](int ss) { return ss == 0 ? pr.idx[0] : pr.idx[1]; };
+    auto valid = [&](int jj, int ss) { return jj < count_of(ss); };
+    auto advance = [&](int& jj, int& ss) {
+      do {
+        if (++ss == kSlots) { ss = 0; ++jj; }
+      } while (jj < steps && !valid(jj, ss));
+    };
+    if (!valid(j, s)) advance(j, s);
+    auto fetch = [&](int jj, int ss) {
+      const int t = __ldg(list_of(ss) + jj);
+      if (lane == 0 && (t < 0 || t >= p.n_tiles))
+        report(p.status, VEDA_STATUS_BAD_INDEX);
+      return clamp_tile(t, p.n_tiles);
+    };
+    int next = j < steps ? fetch(j, s) : 0;
+    while (ok && j < steps) {
+      const int t = next;
+      advance(j, s);
+      if (j < steps) next = fetch(j, s);
+      const int stage = gk % kStages;
+      const uint32_t ph = (gk / kStages) & 1;
+      if (lane == 0) {
+        ok = mbar_wait(&b.k_empty[stage], ph ^ 1, abort, p.status,
+                       VEDA_STATUS_TIMEOUT, p.wait_ns);
+        if (ok && !(p.withhold_first_k && blockIdx.x == 0 && gk == 0)) {
+          mbar_expect_tx(&b.k_full[stage], kKBytes);
+          tma_load_2d(km, smem + kSmemK + stage * kKBytes, &b.k_full[stage],
+                      0, pr.head * n_slots + t * kTile);
+        }
+        if (ok)
+          ok = mbar_wait(&b.v_empty[stage], ph ^ 1, abort, p.status,
                          VEDA_STATUS_TIMEOUT, p.wait_ns);
-          if (ok && !(p.withhold_first_k && blockIdx.x == 0 && gk == 0)) {
-            mbar_expect_tx(&b.k_full[stage], kKBytes);
-            tma_load_2d(km, smem + kSmemK + stage * kKBytes,
-                        &b.k_full[stage], 0, pr.head * n_slots + t * kTile);
-          }
-          if (ok)
-            ok = mbar_wait(&b.v_empty[stage], ph ^ 1, abort, p.status,
-                           VEDA_STATUS_TIMEOUT, p.wait_ns);
-          if (ok) mbar_expect_tx(&b.v_full[stage], kVBytes);
-        }
-        ok = from_lane0(ok);
-        if (!ok) break;
-        ++gk;
-        uint8_t* vdst = smem + kSmemV + stage * kVBytes;
-        if (p.v_perm == nullptr) {
-          if (lane == 0) {
-            tma_load_3d(vm, vdst, &b.v_full[stage], 0, pr.head, t * kTile);
-            tma_load_3d(vm, vdst + kVBytes / 2, &b.v_full[stage], 64,
-                        pr.head, t * kTile);
-          }
-        } else {
-          int y[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int64_t r = __ldg(p.v_perm + static_cast<int64_t>(t) * kTile +
-                                    4 * lane + i);
-            y[i] = (r < 0 || r >= p.seq_len)
-                       ? p.v_rows
-                       : static_cast<int>(r * p.v_heads + v_head);
-          }
-          uint8_t* rows = vdst + 4 * lane * 128;
-          tma_gather4(vm, rows, &b.v_full[stage], 0, y[0], y[1], y[2], y[3]);
-          tma_gather4(vm, rows + kVBytes / 2, &b.v_full[stage], 64, y[0],
-                      y[1], y[2], y[3]);
-        }
-        ++gv;
+        if (ok) mbar_expect_tx(&b.v_full[stage], kVBytes);
       }
+      ok = from_lane0(ok);
+      if (!ok) break;
+      ++gk;
+      if (lane == 0) {
+        uint8_t* vdst = smem + kSmemV + stage * kVBytes;
+        tma_load_3d(vm, vdst, &b.v_full[stage], 0, pr.head, t * kTile);
+        tma_load_3d(vm, vdst + kVBytes / 2, &b.v_full[stage], 64, pr.head,
+                    t * kTile);
+      }
+      ++gv;
     }
   }
   // Let every copy this CTA started land before it can exit.
@@ -985,35 +970,18 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
                               CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
-  const CUtensorMapDataType v_type = v_dtype == VEDA_BF16
-                                         ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  int v_heads = 0;
-  if (perm == nullptr) {  // V in tile order: [slot][head][dim], 64 x 128 boxes
+  {
     const uint64_t dims[3] = {static_cast<uint64_t>(kDim),
                               static_cast<uint64_t>(heads),
                               static_cast<uint64_t>(n_slots)};
     const uint64_t strides[2] = {static_cast<uint64_t>(v_stride_h) * 2,
                                  static_cast<uint64_t>(v_stride_n) * 2};
     const uint32_t box[3] = {64, 1, kTile};
-    if (int rc = encode_tiled(&vm, v_type, 3, v, dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_128B))
-      return rc;
-  } else {  // packed V: rows (s, h) of a [seq_len * v_heads, 128] view
-    if (v_stride_h <= 0 || v_stride_n % v_stride_h != 0)
-      return fail(VEDA_ERR_INVALID,
-                  "packed v needs evenly spaced rows (stride_n a multiple of "
-                  "stride_h); make it contiguous");
-    v_heads = static_cast<int>(v_stride_n / v_stride_h);
-    if (v_heads < heads || seq_len * v_heads >= (1ll << 31) - 1)
-      return fail(VEDA_ERR_INVALID, "packed v: %lld rows x %d heads",
-                  static_cast<long long>(seq_len), v_heads);
-    const uint64_t dims[2] = {static_cast<uint64_t>(kDim),
-                              static_cast<uint64_t>(seq_len) * v_heads};
-    const uint64_t strides[1] = {static_cast<uint64_t>(v_stride_h) * 2};
-    const uint32_t box[2] = {64, 1};
-    if (int rc = encode_tiled(&vm, v_type, 2, v, dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_128B))
+    if (int rc = encode_tiled(
+            &vm,
+            v_dtype == VEDA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+            3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
   // The output as [slot][head][dim], written by TMA in 32 x 32 boxes.
@@ -1047,9 +1015,6 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
   p.perm = perm;
   p.seq_len = seq_len;
   p.out_heads = out_heads;
-  p.v_perm = perm;
-  p.v_heads = v_heads;
-  p.v_rows = static_cast<int>(seq_len * v_heads);
   p.wait_ns = wait_ns;
   p.withhold_first_k = withhold_first_k;
   p.n_tiles = n_tiles;

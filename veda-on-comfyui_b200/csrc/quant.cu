@@ -41,6 +41,12 @@ struct QuantParams {
   // Head group (null: all heads): output head h reads input head heads[h],
   // so one head group of a layer is quantised without copying it out.
   const int32_t* heads;
+  // Packed V (null: none): CTAs with blockIdx.z == 2 copy V rows through
+  // the same permutation and head ids into v_tiled [n_slots, heads, 128]
+  // (tile order, contiguous), the operand layout of the attention kernel.
+  const void* v;
+  int64_t v_stride_n, v_stride_h;  // elements
+  void* v_tiled;
 };
 
 // Eight 16-bit values of one 16-byte load, widened to fp32 (exact).
@@ -91,13 +97,34 @@ __global__ void __launch_bounds__(kQuantThreads, 3)
   __shared__ float pool_sh[POOL ? 8 : 1][3][kDim];
   __shared__ float scale_sh[2], inv_sh[2];
 
-  const QuantJob job = blockIdx.z == 0 ? p.job[0] : p.job[1];
   const int tile = blockIdx.x, head = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int dc = tid & 15;  // dims 8*dc .. 8*dc+7
   const int rg = tid >> 4;  // rows rg + 16 i
-
   const int src_head = p.heads != nullptr ? __ldg(p.heads + head) : head;
+
+  if (blockIdx.z == 2) {  // V: a copy into tile order, no arithmetic
+    const T* v = static_cast<const T*>(p.v) +
+                 static_cast<int64_t>(src_head) * p.v_stride_h + 8 * dc;
+    uint4 r[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t row = __ldg(p.perm + static_cast<int64_t>(tile) * kTile +
+                                rg + 16 * i);
+      r[i] = row >= 0 && row < p.seq_len
+                 ? __ldg(reinterpret_cast<const uint4*>(v + row * p.v_stride_n))
+                 : make_uint4(0, 0, 0, 0);
+    }
+    T* dst = static_cast<T*>(p.v_tiled) +
+             (static_cast<int64_t>(tile) * kTile * gridDim.y + head) * kDim +
+             8 * dc;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(rg + 16 * i) *
+                                          gridDim.y * kDim) = r[i];
+    return;
+  }
+  const QuantJob job = blockIdx.z == 0 ? p.job[0] : p.job[1];
   const T* x = static_cast<const T*>(job.x) +
                static_cast<int64_t>(src_head) * p.stride_h + 8 * dc;
   uint4 raw[8];
@@ -307,7 +334,8 @@ int quant_pool(const void* q, const void* k, int dtype, int64_t stride_n,
                float q_pre_scale, int8_t* q_i8, float* q_scale, int8_t* k_i8,
                float* k_scale, float* feats_q, float* feats_k,
                const int64_t* perm, int64_t seq_len, const int32_t* head_ids,
-               void* stream) {
+               void* stream, const void* v = nullptr, int64_t v_stride_n = 0,
+               int64_t v_stride_h = 0, void* v_tiled = nullptr) {
   if (int rc = check_device()) return rc;
   // packed inputs have seq_len rows; the check wants a whole number of tiles
   const int rows = perm == nullptr ? n_slots : kTile;
@@ -342,7 +370,22 @@ int quant_pool(const void* q, const void* k, int dtype, int64_t stride_n,
   p.perm = perm;
   p.seq_len = seq_len;
   p.heads = head_ids;
-  return launch_quant(p, 2, heads, dtype, static_cast<cudaStream_t>(stream));
+  if ((v == nullptr) != (v_tiled == nullptr))
+    return fail(VEDA_ERR_INVALID, "v and v_tiled go together");
+  if (v != nullptr) {
+    if (perm == nullptr)
+      return fail(VEDA_ERR_INVALID, "a V copy needs packed input (perm)");
+    if (int rc = check_input(v, dtype, v_stride_n, v_stride_h, kTile, heads))
+      return rc;
+    if (!aligned16(v_tiled))
+      return fail(VEDA_ERR_INVALID, "v_tiled must be 16-byte aligned");
+    p.v = v;
+    p.v_stride_n = v_stride_n;
+    p.v_stride_h = v_stride_h;
+    p.v_tiled = v_tiled;
+  }
+  return launch_quant(p, v != nullptr ? 3 : 2, heads, dtype,
+                      static_cast<cudaStream_t>(stream));
 }
 
 }  // namespace
@@ -365,11 +408,12 @@ extern "C" int veda_quant_pool_packed(
     int64_t stride_h, int64_t seq_len, const int64_t* perm, int n_slots,
     int heads, const int32_t* valid_count, int n_video_tiles,
     float q_pre_scale, int8_t* q_i8, float* q_scale, int8_t* k_i8,
-    float* k_scale, float* feats_q, float* feats_k, const int32_t* head_ids,
-    void* stream) {
+    float* k_scale, float* feats_q, float* feats_k, const void* v,
+    int64_t v_stride_n, int64_t v_stride_h, void* v_tiled,
+    const int32_t* head_ids, void* stream) {
   if (perm == nullptr) return fail(VEDA_ERR_INVALID, "null perm");
   return quant_pool(q, k, dtype, stride_n, stride_h, n_slots, heads,
                     valid_count, n_video_tiles, q_pre_scale, q_i8, q_scale,
                     k_i8, k_scale, feats_q, feats_k, perm, seq_len, head_ids,
-                    stream);
+                    stream, v, v_stride_n, v_stride_h, v_tiled);
 }

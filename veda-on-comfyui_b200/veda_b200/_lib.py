@@ -79,7 +79,8 @@ SIGNATURES = {
                                         _I, _P, _P, _I, _I, _P, _P, _L, _L,
                                         _P, _P],
     'veda_quant_pool_packed': [_P, _P, _I, _L, _L, _L, _P, _I, _I, _P, _I,
-                               _F, _P, _P, _P, _P, _P, _P, _P, _P],
+                               _F, _P, _P, _P, _P, _P, _P, _P, _L, _L, _P,
+                               _P, _P],
     'veda_sparse_attention_packed': [_P, _P, _P, _P, _P, _I, _L, _L, _P, _I,
                                      _P, _P, _I, _I, _P, _L, _L, _P, _L, _P,
                                      _P, _P],

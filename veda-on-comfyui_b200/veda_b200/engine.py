@@ -7,11 +7,12 @@ Q, quantise K, cast V, attend, scatter. This fast path does the same call
 in four kernels with no host synchronisation:
 
     quant_pool (Q, K int8 + TripPool features, one read; packed rows are
-                read through the tile permutation)
+                read through the tile permutation, and packed V is copied
+                into tile order by the same launch)
     -> tile_logits (predictor; skipped when scores are given)
     -> select (top-k straight into ascending index lists)
-    -> sparse_attention (tcgen05; packed V is read and the output written
-                         through the permutation)
+    -> sparse_attention (tcgen05; a packed output is written through the
+                         permutation)
 
 `full=True` is a full-attention layer or step (full_attention_layers /
 full_attention_steps, 0% sparsity): the same attention kernel over every
@@ -160,11 +161,12 @@ class VedaAttention:
         [S, H, 128] out in v's dtype.
 
         Each group runs its own kernel sequence on the same packed tensors:
-        Q and K quantised (and pooled) through its permutation and head ids,
-        its scores selected into lists, and its attention reading V and
-        writing its heads of `out` through the permutation. No per-group
-        copy of q, k or v is made, nothing synchronises the host, and the
-        selection counts feed `self.stats`.
+        Q and K quantised (and pooled) and V copied into tile order, all
+        through its permutation and head ids in one launch, its scores
+        selected into lists, and its attention writing its heads of `out`
+        through the permutation. No per-group copy of q, k or v is taken
+        with torch, nothing synchronises the host, and the selection counts
+        feed `self.stats`.
         """
         seq_len, n_heads, dim = q.shape
         device = q.device
@@ -190,7 +192,7 @@ class VedaAttention:
                 scale * kernels.LOG2E, pool=need_pool,
                 out=self._buffers.setdefault(
                     ('group', layout.num_slots, ids32.numel(), device), {}),
-                perm=perm, heads=ids32)
+                perm=perm, heads=ids32, v=v)
             if full:
                 index, count = self._dense_lists(layout, ids32.numel())
             else:
@@ -201,9 +203,10 @@ class VedaAttention:
                 index, count = self.select(scores, layout)
                 self.stats.add_lists(count, layout)
             ops.sparse_attention(quant['q_i8'], quant['q_scale'],
-                                 quant['k_i8'], quant['k_scale'], v, index,
-                                 count, layout.valid_count, out=out,
-                                 perm=perm, heads=ids32)
+                                 quant['k_i8'], quant['k_scale'],
+                                 quant['v_tiled'], index, count,
+                                 layout.valid_count, out=out, perm=perm,
+                                 heads=ids32)
         return out
 
     @torch.no_grad()
@@ -265,10 +268,10 @@ class VedaAttention:
             q_t, k_t, v_t = q, k, v
         else:
             # Packed rows: the quantisation reads Q and K through the
-            # permutation, the attention reads V and writes the output
-            # through it, so nothing is gathered into tile order.
+            # permutation and copies V into tile order in the same launch;
+            # the attention writes the output back through it.
             perm = layout.perm
-            q_t, k_t, v_t = q, k, v
+            q_t, k_t, v_t = q, k, None
         dim = q.shape[-1]
         scale = dim ** -0.5 if self.softmax_scale is None \
             else self.softmax_scale
@@ -283,7 +286,7 @@ class VedaAttention:
                                pool=need_pool,
                                out=self._buffers.setdefault(
                                    (tuple(q_t.shape), q_t.device), {}),
-                               perm=perm)
+                               perm=perm, v=None if tiled_in else v)
         if full:
             index, count = self._dense_lists(layout, heads)
         else:
@@ -309,6 +312,6 @@ class VedaAttention:
             out = torch.empty(q.shape[0], heads, dim, dtype=v.dtype,
                               device=q.device)
         return ops.sparse_attention(quant['q_i8'], quant['q_scale'],
-                                    quant['k_i8'], quant['k_scale'], v_t,
-                                    index, count, layout.valid_count,
-                                    out=out, perm=perm)
+                                    quant['k_i8'], quant['k_scale'],
+                                    quant['v_tiled'], index, count,
+                                    layout.valid_count, out=out, perm=perm)

@@ -126,7 +126,8 @@ def quant_pool(q: torch.Tensor, k: torch.Tensor, valid_count: torch.Tensor,
                n_video_tiles: int, q_pre_scale: float, pool: bool = True,
                out: dict | None = None,
                perm: torch.Tensor | None = None,
-               heads: torch.Tensor | None = None) -> dict:
+               heads: torch.Tensor | None = None,
+               v: torch.Tensor | None = None) -> dict:
     """Fused INT8 quantisation of Q (per 128 rows) and K (per 64 rows) and,
     if `pool`, the [mean | max | min] features of the video tiles.
 
@@ -135,9 +136,12 @@ def quant_pool(q: torch.Tensor, k: torch.Tensor, valid_count: torch.Tensor,
     tile order happens in the same read.
     heads: with `perm`, one head group: [H'] int32 device ids (see
     `head_ids`); output head h holds input head heads[h].
+    v: with `perm`, packed V [S, H, 128] of q's dtype, copied through the
+    same permutation and head ids into `v_tiled` ([slots, H', 128], tile
+    order) by the same launch: the V operand of the attention.
 
-    Returns dict(q_i8, q_scale, k_i8, k_scale, feats_q, feats_k) in tile
-    order; buffers in `out` with those names are reused.
+    Returns dict(q_i8, q_scale, k_i8, k_scale, feats_q, feats_k[, v_tiled])
+    in tile order; buffers in `out` with those names are reused.
     """
     _check_rows(q, 'q')
     _check_rows(k, 'k')
@@ -176,6 +180,15 @@ def quant_pool(q: torch.Tensor, k: torch.Tensor, valid_count: torch.Tensor,
                       torch.float32)
         feats_k = buf('feats_k', (heads, n_video_tiles, 3 * HEAD_DIM),
                       torch.float32)
+    v_tiled = None
+    if v is not None:
+        if perm is None:
+            raise ValueError('a V copy needs packed inputs (perm)')
+        _check_rows(v, 'v')
+        if v.dtype != q.dtype or v.shape[0] != seq_len or \
+                v.device != device:
+            raise ValueError('v must be packed like q (rows, dtype, device)')
+        v_tiled = buf('v_tiled', (n, heads, HEAD_DIM), v.dtype)
     valid = valid_count.to(torch.int32)
     tail = (_ptr(valid), n_video_tiles, ctypes.c_float(q_pre_scale),
             _ptr(q_i8), _ptr(q_scale), _ptr(k_i8), _ptr(k_scale),
@@ -186,8 +199,13 @@ def quant_pool(q: torch.Tensor, k: torch.Tensor, valid_count: torch.Tensor,
     else:
         _call(device, 'veda_quant_pool_packed', _ptr(q), _ptr(k),
               _DTYPES[q.dtype], q.stride(0), q.stride(1), seq_len, _ptr(perm),
-              n, heads, *tail[:-1], _ptr(head_map), tail[-1])
+              n, heads, *tail[:-1], _ptr(v),
+              v.stride(0) if v is not None else 0,
+              v.stride(1) if v is not None else 0, _ptr(v_tiled),
+              _ptr(head_map), tail[-1])
     out['feats_q'], out['feats_k'] = feats_q, feats_k
+    if v_tiled is not None:
+        out['v_tiled'] = v_tiled
     return out
 
 
@@ -286,41 +304,32 @@ def sparse_attention(q_i8, q_scale, k_i8, k_scale, v, index, count,
     out_multicast: the NVSwitch multicast address of `out`'s first element
     (head sharding): rows are stored through it to every GPU bound to the
     multicast object, instead of to `out` alone.
-    perm: packed rows. v is then [S, H, 128] in sequence order and slot i of
-    the tile order reads its row perm[i] (< 0: padding, zeros); `out`
-    ([S, H, 128], required) receives row `slot` of the result at row
-    perm[slot], padding slots dropped. Neither the gather of V nor the
-    scatter of the output is a pass of its own.
-    heads: with `perm`, one head group: list head h reads head heads[h] of v
-    and writes head heads[h] of `out` ([H'] int32 device ids, see
-    `head_ids`).
+    perm: packed output. `out` ([S, H, 128], required) receives row `slot`
+    of the result at row perm[slot]; padding slots (perm < 0) are dropped:
+    the scatter back to sequence order happens in the kernel's epilogue.
+    heads: with `perm`, one head group: head h of v / the lists is written to
+    head heads[h] of `out` ([H'] int32 device ids, see `head_ids`).
     """
     _check_rows(v, 'v')
     device = require_device(q_i8, k_i8, v, index, count, valid_count)
     head_map = heads
-    if head_map is not None and perm is None:
-        raise ValueError('a head group needs packed rows (perm)')
-    if perm is None:
-        n, heads, _ = v.shape
-    else:
-        if out is None or out_multicast:
-            raise ValueError('packed rows need `out` and no multicast')
-        perm = perm.to(device=device, dtype=torch.int64).contiguous()
-        n = perm.numel()
-        heads = v.shape[1] if head_map is None else head_map.numel()
-        if head_map is not None and (head_map.dtype != torch.int32 or
-                                     head_map.device != device):
-            raise ValueError('heads must be int32 ids on the device')
-        if v.shape[0] != out.shape[0]:
-            raise ValueError(f'packed v has {v.shape[0]} rows, out '
-                             f'{out.shape[0]}')
-        if head_map is None and out.shape[1] != v.shape[1]:
-            raise ValueError('out must have v\'s heads')
-        if v.stride(0) % v.stride(1) != 0 or \
-                v.stride(0) // v.stride(1) < v.shape[1]:
-            # the kernel reads packed V as evenly spaced [S * H', 128] rows
-            v = v.contiguous()
+    n, heads, _ = v.shape
     n_tiles = n // TILE
+    if head_map is not None and perm is None:
+        raise ValueError('a head group needs a packed output (perm)')
+    if perm is not None:
+        if out is None or out_multicast:
+            raise ValueError('a packed output needs `out` and no multicast')
+        perm = perm.to(device=device, dtype=torch.int64).contiguous()
+        if perm.numel() != n:
+            raise ValueError('perm must have a slot per row of v')
+        if head_map is not None:
+            if head_map.dtype != torch.int32 or head_map.device != device or \
+                    head_map.numel() != heads:
+                raise ValueError('heads must be int32 ids on the device, one '
+                                 'per head of v')
+        elif out.shape[1] != heads:
+            raise ValueError('out must have v\'s heads')
     if index.shape[0] != heads or count.shape[0] != heads:
         raise ValueError(f'lists for {index.shape[0]} heads, attention over '
                          f'{heads}')
