@@ -26,11 +26,13 @@
 //   warps 4-7    softmax of slot A, warps 8-11 of slot B: one query row per
 //                thread (TMEM lane = row); load the S row, scale, mask,
 //                running max with lazy rescaling of O (only when the max
-//                grows by > 2^8), exp2, write P as packed 16-bit pairs over
-//                the first 64 columns of S; at the end of a tile's walk,
-//                read O out of TMEM (releasing it for the next walk at
-//                once), normalise it and hand it to the TMA in 32 x 32
-//                boxes through a per-warp staging buffer.
+//                grows by > 2^8; after a walk's first tile the exponentials
+//                start at once against the running max and the max is
+//                checked on P afterwards), exp2, write P as packed 16-bit
+//                pairs over the first 64 columns of S; at the end of a
+//                tile's walk, read O out of TMEM (releasing it for the next
+//                walk at once), normalise it and store it through a
+//                per-warp staging buffer as 64-byte row pieces.
 // TMEM: S_A [0, 128), S_B [128, 256), O_A [256, 384), O_B [384, 512); P
 // aliases S. One thread issues every MMA and the tensor pipe runs them in
 // order, so a Q K^T cannot overwrite P before the P V that reads it, and a
@@ -53,7 +55,7 @@ constexpr uint32_t kSmemQ = 0;                  // [slot][buffer] Q tiles
 constexpr uint32_t kSmemK = kSmemQ + 4 * kQBytes;
 constexpr uint32_t kSmemV = kSmemK + kStages * kKBytes;
 // Per softmax warp, 32 rows x 64 bytes: output rows pass through here as
-// 32 x 32 boxes on their way to one asynchronous TMA store each.
+// 32 x 32 boxes on their way to the output as 64-byte row pieces.
 constexpr uint32_t kStageBytes = 32 * 64;
 constexpr uint32_t kSmemStage = kSmemV + kStages * kVBytes;
 constexpr uint32_t kSmemBar = kSmemStage + 8 * kStageBytes;
@@ -422,13 +424,22 @@ __device__ __forceinline__ void store_multicast(void* mc, uint4 u) {
 }
 
 // Columns [32 cc, 32 cc + 32) of the warp's 32 rows (v: this lane's row),
-// staged in shared memory and written as one asynchronous TMA store of the
-// 32 x 32 box (rows row0 .. row0 + 31 of head `head`); the warp waits only
-// until the TMA has read the staging buffer, not for the global write.
+// staged in shared memory to turn them around, then written as 64-byte row
+// pieces, eight rows per instruction, each to its destination row of `out`
+// (dst: element 0 of `out` plus the head offset); rows with dest < 0
+// (padding slots) are dropped. dest[i] is the destination row of row
+// 8 i + lane / 4 of the warp's 32: the tile-order row itself, or
+// perm[slot] for a packed output. Plain stores need no wait before the
+// staging buffer is reused (a TMA store of each box would: ~1,000 SM
+// clocks a box for the TMA to read it back, measured).
 template <typename VT>
-__device__ void store_rows(uint8_t* stage, const CUtensorMap* o_map, int head,
-                           int row0, int cc, int lane, const float* v) {
+__device__ void store_rows(uint8_t* stage, VT* dst, int64_t row_sn,
+                           const int64_t* dest, int cc, int lane,
+                           const float* v) {
+  // 16-byte piece k of row r sits at piece k ^ ((r >> 1) & 3) of the row:
+  // the eight rows of a store phase then cover all 32 banks once
   uint4* mine = reinterpret_cast<uint4*>(stage + lane * 64);
+  const int sw = (lane >> 1) & 3;
 #pragma unroll
   for (int c = 0; c < 32; c += 8) {
     uint4 u;
@@ -436,43 +447,15 @@ __device__ void store_rows(uint8_t* stage, const CUtensorMap* o_map, int head,
     u.y = Pack<VT>::two(v[c + 2], v[c + 3]);
     u.z = Pack<VT>::two(v[c + 4], v[c + 5]);
     u.w = Pack<VT>::two(v[c + 6], v[c + 7]);
-    mine[c / 8] = u;
-  }
-  fence_async_shared();
-  __syncwarp();
-  if (lane == 0) {
-    tma_store_3d(o_map, stage, 32 * cc, head, row0);
-    bulk_commit();
-    bulk_wait_read();
-  }
-  __syncwarp();
-}
-
-// The same box through the packed-output permutation: the staged rows leave
-// as 64-byte pieces, eight rows per instruction, each to row perm[slot] of
-// `out` (dst: element 0 of `out` plus the head offset), padding dropped.
-// dest[i] is the destination row of row 8 i + lane / 4 of the warp's 32.
-template <typename VT>
-__device__ void store_rows_packed(uint8_t* stage, VT* dst, int64_t row_sn,
-                                  const int64_t* dest, int cc, int lane,
-                                  const float* v) {
-  uint4* mine = reinterpret_cast<uint4*>(stage + lane * 64);
-#pragma unroll
-  for (int c = 0; c < 32; c += 8) {
-    uint4 u;
-    u.x = Pack<VT>::two(v[c], v[c + 1]);
-    u.y = Pack<VT>::two(v[c + 2], v[c + 3]);
-    u.z = Pack<VT>::two(v[c + 4], v[c + 5]);
-    u.w = Pack<VT>::two(v[c + 6], v[c + 7]);
-    mine[c / 8] = u;
+    mine[(c / 8) ^ sw] = u;
   }
   __syncwarp();
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int r = 8 * i + (lane >> 2), piece = lane & 3;
     if (dest[i] >= 0) {
-      const uint4 u =
-          *reinterpret_cast<const uint4*>(stage + r * 64 + piece * 16);
+      const uint4 u = *reinterpret_cast<const uint4*>(
+          stage + r * 64 + (piece ^ ((r >> 1) & 3)) * 16);
       *reinterpret_cast<uint4*>(dst + dest[i] * row_sn + 32 * cc +
                                 8 * piece) = u;
     }
@@ -496,6 +479,7 @@ struct TileMeta {
 // The only rounding beyond the reference's fp32 product is that of
 // off + m, at most 0.75 units of S, against the ~10^2 units of noise the
 // INT8 quantisation itself puts into S.
+constexpr float kRescaleFactor = 256.0f;  // 2^kRescaleThreshold
 constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
 constexpr uint32_t kMaskBits = 0xFF800000u - kMagicBits;
@@ -522,8 +506,8 @@ __device__ __forceinline__ bool wait_published(const int* counter, int walks,
   return true;
 }
 
-// 16 bytes from global memory through L2 only (rows this CTA's TMA stores
-// just wrote; nothing of them sits in L1).
+// 16 bytes from global memory through L2 only (rows this CTA's softmax
+// warps just stored, behind a fence).
 __device__ __forceinline__ uint4 ld_cg_v4(const void* ptr) {
   uint4 u;
   asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -533,8 +517,8 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* ptr) {
 }
 
 // Warps 2 and 3, head-sharded output only: the pusher of slot s. The
-// softmax warps write their rows to this GPU's copy of the output (TMA
-// stores) and publish each walk per TMEM quarter; the pusher reads the
+// softmax warps write their rows to this GPU's copy of the output and
+// publish each walk per TMEM quarter; the pusher reads the
 // published rows back (from L2) and writes them through the multicast
 // address, so NVSwitch delivers them to every GPU while the next walks
 // compute. Rows are never rewritten within a launch, so the pusher may lag.
@@ -581,8 +565,8 @@ __device__ void push_slot(int s, Barriers& b, const AttnParams& p, int lane) {
 
 template <typename VT>
 __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
-                             uint32_t tmem, const AttnParams& p,
-                             const CUtensorMap* o_map, int warp, int lane) {
+                             uint32_t tmem, const AttnParams& p, int warp,
+                             int lane) {
   volatile int* abort = &b.abort;
   uint8_t* stage = smem + kSmemStage + (warp - 4) * kStageBytes;
   const int quarter = warp & 3;  // TMEM lanes this warp may access
@@ -592,16 +576,16 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
   int tiles = 0, items = 0;  // phases of s_full / o_ready of this slot
   bool good = true;
   // Head-sharded output: a walk's rows are published to the pusher warp
-  // once their TMA stores have completed. That wait is put off until the
-  // next walk's first S, a pair this slot has no work in, or the end.
+  // after the warp's stores of them, behind a fence, so the pusher's reads
+  // through L2 see them. The publication is put off until the next walk's
+  // first S, a pair this slot has no work in, or the end.
   const bool sharded = p.out_mc != nullptr;
   bool unpublished = false;
   auto publish = [&]() {
     if (!unpublished) return;
+    __threadfence();
+    __syncwarp();
     if (lane == 0) {
-      bulk_wait();
-      fence_async_global();
-      __threadfence_block();
       volatile int* n = &b.published[slot][quarter];
       *n = *n + 1;
     }
@@ -614,20 +598,24 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
     if (qt >= p.n_tiles) continue;
     const int count = pr.count[slot];
     const int head = pr.head;
-    // the warp's first row: the output map's row coordinate
+    // the warp's first row (tile order)
     const int row0 = qt * kTile + quarter * 32;
-    // packed output: the destination rows of this lane's four row pieces
-    int64_t dest[4] = {-1, -1, -1, -1};
-    if (p.perm != nullptr) {
+    // the destination rows of this lane's four row pieces: the rows
+    // themselves, or through the permutation for a packed output
+    int64_t dest[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int64_t d = __ldg(p.perm + row0 + 8 * i + (lane >> 2));
+    for (int i = 0; i < 4; ++i) {
+      const int row = row0 + 8 * i + (lane >> 2);
+      if (p.perm != nullptr) {
+        const int64_t d = __ldg(p.perm + row);
         dest[i] = d < p.seq_len ? d : -1;
+      } else {
+        dest[i] = row;
       }
     }
     const int out_head = p.out_heads != nullptr ? __ldg(p.out_heads + head)
                                                 : head;
-    VT* packed =
+    VT* dst =
         static_cast<VT*>(p.out) + static_cast<int64_t>(out_head) * p.out_sh;
     if (count == 0) {  // nothing kept: the reference's acc / 1 = 0
       publish();
@@ -636,10 +624,7 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
       for (int c = 0; c < 32; ++c) zero[c] = 0.0f;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc)
-        if (p.perm != nullptr)
-          store_rows_packed<VT>(stage, packed, p.out_sn, dest, cc, lane, zero);
-        else
-          store_rows<VT>(stage, o_map, head, row0, cc, lane, zero);
+        store_rows<VT>(stage, dst, p.out_sn, dest, cc, lane, zero);
       unpublished = sharded;
       continue;
     }
@@ -681,60 +666,92 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
       if (j == 0) publish();
       tc_fence_after();
       uint32_t r[128];
-      tmem_ld32(s_addr + 0, r);
-      tmem_ld32(s_addr + 32, r + 32);
-      tmem_ld32(s_addr + 64, r + 64);
-      tmem_ld32(s_addr + 96, r + 96);
-      tmem_ld_wait(r);
-      reg_fence32(r + 32);
-      reg_fence32(r + 64);
-      reg_fence32(r + 96);
-      // valid is the tile's (the same in every lane): a warp-uniform branch.
-      // Masked columns get kMaskBits: never the integer max (every real S
-      // is above -2^21), and -inf once the bias is added.
-      if (__any_sync(0xffffffffu, cur.valid < kTile)) {
+      // S of this tile into registers; masked columns (at or past the
+      // tile's valid rows, the same in every lane: a warp-uniform branch)
+      // get kMaskBits, which is -inf once the bias is added, so they never
+      // win the row max and their exponential is 0.
+      auto load_s = [&]() {
+        tmem_ld32(s_addr + 0, r);
+        tmem_ld32(s_addr + 32, r + 32);
+        tmem_ld32(s_addr + 64, r + 64);
+        tmem_ld32(s_addr + 96, r + 96);
+        tmem_ld_wait(r);
+        reg_fence32(r + 32);
+        reg_fence32(r + 64);
+        reg_fence32(r + 96);
+        if (__any_sync(0xffffffffu, cur.valid < kTile)) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c >= cur.valid) r[c] = kMaskBits;
-      }
-      // row max of each 64-column half on the raw int32 S (the biased
-      // values are monotone in S, so the bias is added to the two maxima
-      // here and to every value in the exponential pass below)
-      int ia0 = INT_MIN, ib0 = INT_MIN, ia1 = INT_MIN, ib1 = INT_MIN;
-#pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        ia0 = max(ia0, static_cast<int>(r[c]));
-        ib0 = max(ib0, static_cast<int>(r[c + 1]));
-        ia1 = max(ia1, static_cast<int>(r[c + 64]));
-        ib1 = max(ib1, static_cast<int>(r[c + 65]));
-      }
-      const uint32_t top0 = static_cast<uint32_t>(max(ia0, ib0)) + kMagicBits;
-      const uint32_t top1 = static_cast<uint32_t>(max(ia1, ib1)) + kMagicBits;
-      const float mt = fmaxf(fmaf(__uint_as_float(top0), cur.sc0, -cur.off0),
-                             fmaf(__uint_as_float(top1), cur.sc1, -cur.off1));
-      const bool need = mt > m + kRescaleThreshold;
+          for (int c = 0; c < 128; ++c)
+            if (c >= cur.valid) r[c] = kMaskBits;
+        }
+      };
+      // Row max on the biased values (r + kMagicBits read as fp32, monotone
+      // in S) of each 64-column half, scaled afterwards; the max grows m
+      // only by more than kRescaleThreshold (lazy rescaling of O).
+      bool need = false;
       float alpha = 1.0f;
-      if (need) {
-        alpha = ex2_approx(m - mt);
-        m = mt;
-        l *= alpha;
-      }
-      const uint64_t s0 = f2(cur.sc0, cur.sc0), s1 = f2(cur.sc1, cur.sc1);
-      const float c0 = -(cur.off0 + m), c1 = -(cur.off1 + m);
-      const uint64_t n0 = f2(c0, c0), n1 = f2(c1, c1);
-      uint64_t acc[4] = {0, 0, 0, 0};
-      uint32_t pk[64];
+      auto max_pass = [&]() {
+        float top0 = -INFINITY, top1 = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const uint64_t z =
-            fma2(f2(__uint_as_float(r[2 * i] + kMagicBits),
-                    __uint_as_float(r[2 * i + 1] + kMagicBits)),
-                 i < 32 ? s0 : s1, i < 32 ? n0 : n1);
-        float z0, z1;
-        f2_split(z, z0, z1);
-        const float p0 = ex2_approx(z0), p1 = ex2_approx(z1);
-        acc[i & 3] = add2(acc[i & 3], f2(p0, p1));
-        pk[i] = Pack<VT>::two(p0, p1);
+        for (int i = 0; i < 64; ++i) {
+          const float b0 = __uint_as_float(r[2 * i] + kMagicBits);
+          const float b1 = __uint_as_float(r[2 * i + 1] + kMagicBits);
+          if (i < 32)
+            top0 = max3(top0, b0, b1);
+          else
+            top1 = max3(top1, b0, b1);
+        }
+        const float mt = fmaxf(fmaf(top0, cur.sc0, -cur.off0),
+                               fmaf(top1, cur.sc1, -cur.off1));
+        need = mt > m + kRescaleThreshold;
+        if (need) {
+          alpha = ex2_approx(m - mt);
+          m = mt;
+          l *= alpha;
+        }
+      };
+      const uint64_t s0 = f2(cur.sc0, cur.sc0), s1 = f2(cur.sc1, cur.sc1);
+      uint64_t acc[4];
+      uint32_t pk[64];
+      float pmax = 0.0f;
+      auto exp_pass = [&](auto track) {
+        const float c0 = -(cur.off0 + m), c1 = -(cur.off1 + m);
+        const uint64_t n0 = f2(c0, c0), n1 = f2(c1, c1);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[q] = 0;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const uint64_t z =
+              fma2(f2(__uint_as_float(r[2 * i] + kMagicBits),
+                      __uint_as_float(r[2 * i + 1] + kMagicBits)),
+                   i < 32 ? s0 : s1, i < 32 ? n0 : n1);
+          float z0, z1;
+          f2_split(z, z0, z1);
+          const float p0 = ex2_approx(z0), p1 = ex2_approx(z1);
+          acc[i & 3] = add2(acc[i & 3], f2(p0, p1));
+          if constexpr (decltype(track)::value) pmax = max3(pmax, p0, p1);
+          pk[i] = Pack<VT>::two(p0, p1);
+        }
+      };
+      load_s();
+      if (j == 0) {
+        // first tile of a walk: the max comes first
+        max_pass();
+        exp_pass(std::false_type{});
+      } else {
+        // later tiles: P at once against the running max, the largest P
+        // tracked alongside; only if it passes 2^kRescaleThreshold (rare
+        // once a walk is under way) is S read again (TMEM still holds it:
+        // P is stored over it only below), its max taken and P computed
+        // against that. The whole warp redoes it, so no lane keeps its
+        // first P beside the reload; a lane whose max held gets the same
+        // bits again.
+        exp_pass(std::true_type{});
+        if (__any_sync(0xffffffffu, pmax > kRescaleFactor)) {
+          load_s();
+          max_pass();
+          exp_pass(std::false_type{});
+        }
       }
       tmem_st32(s_addr + 0, pk);
       tmem_st32(s_addr + 32, pk + 32);
@@ -804,16 +821,11 @@ __device__ void softmax_loop(int slot, uint8_t* smem, Barriers& b,
       float v[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(o[32 * cc + c]) * inv;
-      if (p.perm != nullptr)
-        store_rows_packed<VT>(stage, packed, p.out_sn, dest, cc, lane, v);
-      else
-        store_rows<VT>(stage, o_map, head, row0, cc, lane, v);
+      store_rows<VT>(stage, dst, p.out_sn, dest, cc, lane, v);
     }
     unpublished = sharded;
   }
   if (good) publish();
-  // The TMA stores have written their rows before the CTA exits.
-  if (lane == 0) bulk_wait();
 }
 
 template <uint32_t N>
@@ -830,7 +842,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     sparse_attention_kernel(const __grid_constant__ CUtensorMap q_map,
                             const __grid_constant__ CUtensorMap k_map,
                             const __grid_constant__ CUtensorMap v_map,
-                            const __grid_constant__ CUtensorMap o_map,
                             const AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   Barriers& b = *reinterpret_cast<Barriers*>(smem + kSmemBar);
@@ -881,7 +892,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else {
     regs_inc<kHighRegs>();
     if (run)
-      softmax_loop<VT>((warp - 4) >> 2, smem, b, tmem, p, &o_map, warp, lane);
+      softmax_loop<VT>((warp - 4) >> 2, smem, b, tmem, p, warp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -896,8 +907,7 @@ std::atomic<int> g_sm_count[64];
 
 template <typename VT>
 int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
-           const CUtensorMap& om, const AttnParams& p, cudaStream_t stream,
-           int dt) {
+           const AttnParams& p, cudaStream_t stream, int dt) {
   const int device = current_device();
   int sms = 148;
   if (device >= 0 && device < 64 && g_sm_count[device].load() > 0) {
@@ -915,7 +925,7 @@ int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
   }
   const int grid = p.n_pairs < sms ? p.n_pairs : sms;
   sparse_attention_kernel<VT><<<grid, kAttnThreads, kSmemBytes, stream>>>(
-      qm, km, vm, om, p);
+      qm, km, vm, p);
   VEDA_CHECK_CUDA(cudaGetLastError());
   return VEDA_OK;
 }
@@ -984,24 +994,6 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
             3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
-  // The output as [slot][head][dim], written by TMA in 32 x 32 boxes.
-  CUtensorMap om;
-  {
-    // (over the packed rows when the output is packed: the map is then
-    // not used, and must not reach past them)
-    const uint64_t dims[3] = {
-        static_cast<uint64_t>(kDim), static_cast<uint64_t>(heads),
-        static_cast<uint64_t>(perm != nullptr ? seq_len : n_slots)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(out_stride_h) * 2,
-                                 static_cast<uint64_t>(out_stride_n) * 2};
-    const uint32_t box[3] = {32, 1, 32};
-    if (int rc = encode_tiled(
-            &om,
-            v_dtype == VEDA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-            3, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return rc;
-  }
   AttnParams p{};
   p.q_scale = q_scale;
   p.k_scale = k_scale;
@@ -1024,8 +1016,8 @@ int attend(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8,
   p.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (v_dtype == VEDA_BF16)
-    return launch<__nv_bfloat16>(qm, km, vm, om, p, s, 0);
-  return launch<__half>(qm, km, vm, om, p, s, 1);
+    return launch<__nv_bfloat16>(qm, km, vm, p, s, 0);
+  return launch<__half>(qm, km, vm, p, s, 1);
 }
 
 }  // namespace
