@@ -32,6 +32,7 @@ struct QuantParams {
   QuantJob job[2];
   int64_t stride_n, stride_h;  // elements
   int n_tiles;
+  int n_heads;                 // output heads of the launch
   const int32_t* valid;        // [n_tiles] or null (all 128)
   int n_video;
   // Packed input (null: rows already in tile order): slot -> packed row,
@@ -85,197 +86,239 @@ __device__ __forceinline__ int8_t quant_one(float x, float b, float y) {
 }
 
 // The tile is held as raw 16-bit words (32 registers a thread) and widened
-// twice, once for the block max and once for the codes, so three CTAs fit
-// on an SM and more loads are in flight. POOL adds the TripPool features;
-// their accumulators would leave room for two CTAs only, so the pooling
-// variant reads its tile a second time for the codes (an L2 hit: the tile
-// was read microseconds earlier by the same CTA) and keeps three.
-template <typename T, bool POOL>
-__global__ void __launch_bounds__(kQuantThreads, 3)
+// twice, once for the block max and once for the codes. POOL adds the
+// TripPool features; their accumulators leave room for few CTAs, so the
+// pooling variant reads its tile a second time for the codes (an L2 hit:
+// the tile was read microseconds earlier by the same CTA) and keeps three
+// CTAs per SM. Without pooling a CTA takes HEADS heads of one tile: their
+// loads are all issued before any arithmetic (16 row loads in flight per
+// thread), and a packed tile's permutation rows are read once for them.
+template <typename T, bool POOL, int HEADS>
+__global__ void __launch_bounds__(kQuantThreads, POOL ? 3 : 2)
     quant_pool_kernel(const QuantParams p) {
   __shared__ float amax_sh[8][2];
   __shared__ float pool_sh[POOL ? 8 : 1][3][kDim];
   __shared__ float scale_sh[2], inv_sh[2];
 
-  const int tile = blockIdx.x, head = blockIdx.y;
+  const int tile = blockIdx.x;
+  const int n_heads = p.n_heads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int dc = tid & 15;  // dims 8*dc .. 8*dc+7
   const int rg = tid >> 4;  // rows rg + 16 i
-  const int src_head = p.heads != nullptr ? __ldg(p.heads + head) : head;
+  int head_of[HEADS], src_of[HEADS];
+#pragma unroll
+  for (int hh = 0; hh < HEADS; ++hh) {
+    head_of[hh] = blockIdx.y * HEADS + hh;
+    const int h = head_of[hh] < n_heads ? head_of[hh] : n_heads - 1;
+    src_of[hh] = p.heads != nullptr ? __ldg(p.heads + h) : h;
+  }
+  // the tile's rows in the input (the permutation, or the rows themselves)
+  int64_t rows[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t slot = static_cast<int64_t>(tile) * kTile + rg + 16 * i;
+    rows[i] = p.perm != nullptr ? __ldg(p.perm + slot) : slot;
+  }
+  auto live_row = [&](int64_t row) {
+    return row >= 0 && (p.perm == nullptr || row < p.seq_len);
+  };
 
   if (blockIdx.z == 2) {  // V: a copy into tile order, no arithmetic
-    const T* v = static_cast<const T*>(p.v) +
-                 static_cast<int64_t>(src_head) * p.v_stride_h + 8 * dc;
-    uint4 r[8];
+    uint4 r[HEADS][8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int64_t row = __ldg(p.perm + static_cast<int64_t>(tile) * kTile +
-                                rg + 16 * i);
-      r[i] = row >= 0 && row < p.seq_len
-                 ? __ldg(reinterpret_cast<const uint4*>(v + row * p.v_stride_n))
-                 : make_uint4(0, 0, 0, 0);
+    for (int hh = 0; hh < HEADS; ++hh) {
+      const T* v = static_cast<const T*>(p.v) +
+                   static_cast<int64_t>(src_of[hh]) * p.v_stride_h + 8 * dc;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        r[hh][i] = live_row(rows[i])
+                       ? __ldg(reinterpret_cast<const uint4*>(
+                             v + rows[i] * p.v_stride_n))
+                       : make_uint4(0, 0, 0, 0);
     }
-    T* dst = static_cast<T*>(p.v_tiled) +
-             (static_cast<int64_t>(tile) * kTile * gridDim.y + head) * kDim +
-             8 * dc;
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(rg + 16 * i) *
-                                          gridDim.y * kDim) = r[i];
+    for (int hh = 0; hh < HEADS; ++hh) {
+      if (head_of[hh] >= n_heads) continue;
+      T* dst = static_cast<T*>(p.v_tiled) +
+               (static_cast<int64_t>(tile) * kTile * n_heads + head_of[hh]) *
+                   kDim + 8 * dc;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(rg + 16 * i) *
+                                            n_heads * kDim) = r[hh][i];
+    }
     return;
   }
   const QuantJob job = blockIdx.z == 0 ? p.job[0] : p.job[1];
-  const T* x = static_cast<const T*>(job.x) +
-               static_cast<int64_t>(src_head) * p.stride_h + 8 * dc;
-  uint4 raw[8];
+  uint4 raw[HEADS][8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    int64_t row = static_cast<int64_t>(tile) * kTile + rg + 16 * i;
-    if (p.perm != nullptr) row = __ldg(p.perm + row);
-    raw[i] = row >= 0 && (p.perm == nullptr || row < p.seq_len)
-                 ? __ldg(reinterpret_cast<const uint4*>(x + row * p.stride_n))
-                 : make_uint4(0, 0, 0, 0);
+  for (int hh = 0; hh < HEADS; ++hh) {
+    const T* x = static_cast<const T*>(job.x) +
+                 static_cast<int64_t>(src_of[hh]) * p.stride_h + 8 * dc;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      raw[hh][i] = live_row(rows[i])
+                       ? __ldg(reinterpret_cast<const uint4*>(
+                             x + rows[i] * p.stride_n))
+                       : make_uint4(0, 0, 0, 0);
   }
   const float pre = job.pre_scale;
-
-  // TripPool over the real rows (a prefix of the tile), before pre-scaling,
-  // and max |x * pre| of rows 0-63 (a[0]) and 64-127 (a[1]).
-  const bool pool = POOL && job.feats != nullptr && tile < p.n_video;
-  const int valid = POOL && p.valid != nullptr ? __ldg(p.valid + tile) : kTile;
-  float s[8], mx[8], mn[8];
-  if (POOL) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      s[e] = 0.0f;
-      mx[e] = -INFINITY;
-      mn[e] = INFINITY;
-    }
-  }
-  float a[2] = {0.0f, 0.0f};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float f[8];
-    unpack8(raw[i], f, T());
-    if (POOL && pool && rg + 16 * i < valid) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        s[e] += f[e];
-        mx[e] = fmaxf(mx[e], f[e]);
-        mn[e] = fminf(mn[e], f[e]);
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      a[i >> 2] = fmaxf(a[i >> 2], fabsf(__fmul_rn(f[e], pre)));
-  }
-  if (POOL && pool) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      s[e] += __shfl_xor_sync(0xffffffffu, s[e], 16);
-      mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
-      mn[e] = fminf(mn[e], __shfl_xor_sync(0xffffffffu, mn[e], 16));
-    }
-    if (lane < 16) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        pool_sh[warp][0][8 * dc + e] = s[e];
-        pool_sh[warp][1][8 * dc + e] = mx[e];
-        pool_sh[warp][2][8 * dc + e] = mn[e];
-      }
-    }
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    a[0] = fmaxf(a[0], __shfl_xor_sync(0xffffffffu, a[0], off));
-    a[1] = fmaxf(a[1], __shfl_xor_sync(0xffffffffu, a[1], off));
-  }
-  if (lane == 0) {
-    amax_sh[warp][0] = a[0];
-    amax_sh[warp][1] = a[1];
-  }
-  __syncthreads();
-  if (tid < 2) {
-    float m0 = 0.0f, m1 = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      m0 = fmaxf(m0, amax_sh[w][0]);
-      m1 = fmaxf(m1, amax_sh[w][1]);
-    }
-    float m = tid == 0 ? m0 : m1;
-    if (job.block == kTile) m = fmaxf(m0, m1);
-    float sc = __fdiv_rn(m, 127.0f);
-    sc = sc > 0.0f ? sc : 1.0f;
-    scale_sh[tid] = sc;
-    inv_sh[tid] = __frcp_rn(sc);
-  }
-  if (POOL && pool && tid < kDim) {
-    float sum = 0.0f, hi = -INFINITY, lo = INFINITY;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      sum += pool_sh[w][0][tid];
-      hi = fmaxf(hi, pool_sh[w][1][tid]);
-      lo = fminf(lo, pool_sh[w][2][tid]);
-    }
-    float* f = job.feats + (static_cast<int64_t>(head) * p.n_video + tile) * 3 * kDim;
-    const bool live = valid > 0;
-    f[tid] = live ? __fdiv_rn(sum, static_cast<float>(valid)) : 0.0f;
-    f[kDim + tid] = live ? hi : 0.0f;
-    f[2 * kDim + tid] = live ? lo : 0.0f;
-  }
-  __syncthreads();
-
-  const float sc[2] = {scale_sh[0], scale_sh[1]};
-  const float inv[2] = {inv_sh[0], inv_sh[1]};
   const int64_t n_slots = static_cast<int64_t>(p.n_tiles) * kTile;
-  int8_t* out = job.out + (static_cast<int64_t>(head) * n_slots +
-                           static_cast<int64_t>(tile) * kTile) * kDim + 8 * dc;
+
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float b = sc[i >> 2], y = inv[i >> 2];
-    float f[8];
+  for (int hh = 0; hh < HEADS; ++hh) {
+    const int head = head_of[hh];
+    if (head >= n_heads) break;  // the same in every thread of the CTA
+    if (hh > 0) __syncthreads();  // the last head's reductions are read
+    // TripPool over the real rows (a prefix of the tile), before
+    // pre-scaling, and max |x * pre| of rows 0-63 (a[0]) and 64-127 (a[1]).
+    const bool pool = POOL && job.feats != nullptr && tile < p.n_video;
+    const int valid =
+        POOL && p.valid != nullptr ? __ldg(p.valid + tile) : kTile;
+    float s[8], mx[8], mn[8];
     if (POOL) {
-      int64_t row = static_cast<int64_t>(tile) * kTile + rg + 16 * i;
-      if (p.perm != nullptr) row = __ldg(p.perm + row);
-      raw[i] = row >= 0 && (p.perm == nullptr || row < p.seq_len)
-                   ? __ldg(reinterpret_cast<const uint4*>(x + row * p.stride_n))
-                   : make_uint4(0, 0, 0, 0);
-    }
-    unpack8(raw[i], f, T());
-    uint32_t lo = 0, hi = 0;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      lo |= static_cast<uint32_t>(static_cast<uint8_t>(
-                quant_one(__fmul_rn(f[e], pre), b, y))) << (8 * e);
-      hi |= static_cast<uint32_t>(static_cast<uint8_t>(
-                quant_one(__fmul_rn(f[e + 4], pre), b, y))) << (8 * e);
+      for (int e = 0; e < 8; ++e) {
+        s[e] = 0.0f;
+        mx[e] = -INFINITY;
+        mn[e] = INFINITY;
+      }
     }
-    *reinterpret_cast<uint2*>(out + (rg + 16 * i) * kDim) = make_uint2(lo, hi);
-  }
-  if (tid == 0) {
-    if (job.block == kTile) {
-      job.scale[static_cast<int64_t>(head) * p.n_tiles + tile] = sc[0];
-    } else {
-      float* sp = job.scale + static_cast<int64_t>(head) * 2 * p.n_tiles + 2 * tile;
-      sp[0] = sc[0];
-      sp[1] = sc[1];
+    float a[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float f[8];
+      unpack8(raw[hh][i], f, T());
+      if (POOL && pool && rg + 16 * i < valid) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          s[e] += f[e];
+          mx[e] = fmaxf(mx[e], f[e]);
+          mn[e] = fminf(mn[e], f[e]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        a[i >> 2] = fmaxf(a[i >> 2], fabsf(__fmul_rn(f[e], pre)));
+    }
+    if (POOL && pool) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        s[e] += __shfl_xor_sync(0xffffffffu, s[e], 16);
+        mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
+        mn[e] = fminf(mn[e], __shfl_xor_sync(0xffffffffu, mn[e], 16));
+      }
+      if (lane < 16) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pool_sh[warp][0][8 * dc + e] = s[e];
+          pool_sh[warp][1][8 * dc + e] = mx[e];
+          pool_sh[warp][2][8 * dc + e] = mn[e];
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      a[0] = fmaxf(a[0], __shfl_xor_sync(0xffffffffu, a[0], off));
+      a[1] = fmaxf(a[1], __shfl_xor_sync(0xffffffffu, a[1], off));
+    }
+    if (lane == 0) {
+      amax_sh[warp][0] = a[0];
+      amax_sh[warp][1] = a[1];
+    }
+    __syncthreads();
+    if (tid < 2) {
+      float m0 = 0.0f, m1 = 0.0f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        m0 = fmaxf(m0, amax_sh[w][0]);
+        m1 = fmaxf(m1, amax_sh[w][1]);
+      }
+      float m = tid == 0 ? m0 : m1;
+      if (job.block == kTile) m = fmaxf(m0, m1);
+      float sc = __fdiv_rn(m, 127.0f);
+      sc = sc > 0.0f ? sc : 1.0f;
+      scale_sh[tid] = sc;
+      inv_sh[tid] = __frcp_rn(sc);
+    }
+    if (POOL && pool && tid < kDim) {
+      float sum = 0.0f, hi = -INFINITY, lo = INFINITY;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        sum += pool_sh[w][0][tid];
+        hi = fmaxf(hi, pool_sh[w][1][tid]);
+        lo = fminf(lo, pool_sh[w][2][tid]);
+      }
+      float* f = job.feats +
+                 (static_cast<int64_t>(head) * p.n_video + tile) * 3 * kDim;
+      const bool live = valid > 0;
+      f[tid] = live ? __fdiv_rn(sum, static_cast<float>(valid)) : 0.0f;
+      f[kDim + tid] = live ? hi : 0.0f;
+      f[2 * kDim + tid] = live ? lo : 0.0f;
+    }
+    __syncthreads();
+
+    const float sc[2] = {scale_sh[0], scale_sh[1]};
+    const float inv[2] = {inv_sh[0], inv_sh[1]};
+    int8_t* out = job.out + (static_cast<int64_t>(head) * n_slots +
+                             static_cast<int64_t>(tile) * kTile) * kDim +
+                  8 * dc;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float b = sc[i >> 2], y = inv[i >> 2];
+      float f[8];
+      if (POOL) {
+        const T* x = static_cast<const T*>(job.x) +
+                     static_cast<int64_t>(src_of[hh]) * p.stride_h + 8 * dc;
+        raw[hh][i] = live_row(rows[i])
+                         ? __ldg(reinterpret_cast<const uint4*>(
+                               x + rows[i] * p.stride_n))
+                         : make_uint4(0, 0, 0, 0);
+      }
+      unpack8(raw[hh][i], f, T());
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        lo |= static_cast<uint32_t>(static_cast<uint8_t>(
+                  quant_one(__fmul_rn(f[e], pre), b, y))) << (8 * e);
+        hi |= static_cast<uint32_t>(static_cast<uint8_t>(
+                  quant_one(__fmul_rn(f[e + 4], pre), b, y))) << (8 * e);
+      }
+      *reinterpret_cast<uint2*>(out + (rg + 16 * i) * kDim) =
+          make_uint2(lo, hi);
+    }
+    if (tid == 0) {
+      if (job.block == kTile) {
+        job.scale[static_cast<int64_t>(head) * p.n_tiles + tile] = sc[0];
+      } else {
+        float* sp =
+            job.scale + static_cast<int64_t>(head) * 2 * p.n_tiles + 2 * tile;
+        sp[0] = sc[0];
+        sp[1] = sc[1];
+      }
     }
   }
 }
 
-int launch_quant(const QuantParams& p, int n_jobs, int heads, int dtype,
+int launch_quant(QuantParams p, int n_jobs, int heads, int dtype,
                  cudaStream_t stream) {
-  dim3 grid(p.n_tiles, heads, n_jobs);
+  p.n_heads = heads;
   const bool pool = p.job[0].feats != nullptr && p.n_video > 0;
+  // two heads per CTA without pooling, one with it
+  const dim3 grid(p.n_tiles, pool ? heads : (heads + 1) / 2, n_jobs);
   if (dtype == VEDA_BF16) {
     if (pool)
-      quant_pool_kernel<__nv_bfloat16, true><<<grid, kQuantThreads, 0, stream>>>(p);
+      quant_pool_kernel<__nv_bfloat16, true, 1>
+          <<<grid, kQuantThreads, 0, stream>>>(p);
     else
-      quant_pool_kernel<__nv_bfloat16, false><<<grid, kQuantThreads, 0, stream>>>(p);
+      quant_pool_kernel<__nv_bfloat16, false, 2>
+          <<<grid, kQuantThreads, 0, stream>>>(p);
   } else {
     if (pool)
-      quant_pool_kernel<__half, true><<<grid, kQuantThreads, 0, stream>>>(p);
+      quant_pool_kernel<__half, true, 1><<<grid, kQuantThreads, 0, stream>>>(p);
     else
-      quant_pool_kernel<__half, false><<<grid, kQuantThreads, 0, stream>>>(p);
+      quant_pool_kernel<__half, false, 2>
+          <<<grid, kQuantThreads, 0, stream>>>(p);
   }
   VEDA_CHECK_CUDA(cudaGetLastError());
   return VEDA_OK;
