@@ -87,3 +87,31 @@ def test_packed_output_equals_attention_then_scatter(cuda_device, dtype):
     ops.sparse_attention(*args, out=got, perm=layout.perm)
     ops.check_status(cuda_device)
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize('pool', [False, True])
+def test_packed_quantisation_of_an_odd_head_group(cuda_device, pool):
+    """Three heads of four, in a scrambled order: the two-heads-per-CTA
+    launch leaves its last CTA's second head out. Codes, scales, features
+    and the V copy equal gather_tiles then quantisation of the same heads."""
+    from veda_b200 import kernels, ops
+    case = problems.CASES['gpu_problem']
+    layout = helpers.device_layout(case, cuda_device)
+    q, k, v = _packed(case, torch.bfloat16, cuda_device)
+    n_heads = q.shape[1]
+    group = [2, 0, 3][:max(1, n_heads - 1)]
+    ids32 = ops.head_ids(group, n_heads, cuda_device)
+    ids64 = ids32.to(torch.int64)
+    pre = 128 ** -0.5 * kernels.LOG2E
+    n_video = layout.n_video_tiles if pool else 0
+    want = ops.quant_pool(ops.gather_tiles(q, layout.perm, ids64),
+                          ops.gather_tiles(k, layout.perm, ids64),
+                          layout.valid_count, n_video, pre, pool=pool)
+    got = ops.quant_pool(q, k, layout.valid_count, n_video, pre, pool=pool,
+                         perm=layout.perm, heads=ids32, v=v)
+    ops.check_status(cuda_device)
+    keys = ['q_i8', 'q_scale', 'k_i8', 'k_scale'] + \
+        (['feats_q', 'feats_k'] if pool else [])
+    for key in keys:
+        assert torch.equal(got[key], want[key]), key
+    assert torch.equal(got['v_tiled'], ops.gather_tiles(v, layout.perm, ids64))
