@@ -71,6 +71,36 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* f, __half) {
   }
 }
 
+// Element-wise max / min of two packed pairs of 16-bit values, in their own
+// format (the order of the widened fp32 values, exactly), and the packed
+// pairs of -inf / +inf that start a running max / min.
+__device__ __forceinline__ uint32_t max2(uint32_t a, uint32_t b,
+                                         __nv_bfloat16) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b,
+                                         __nv_bfloat16) {
+  uint32_t d;
+  asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t max2(uint32_t a, uint32_t b, __half) {
+  uint32_t d;
+  asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b, __half) {
+  uint32_t d;
+  asm("min.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t neg_inf2(__nv_bfloat16) { return 0xFF80FF80u; }
+__device__ __forceinline__ uint32_t pos_inf2(__nv_bfloat16) { return 0x7F807F80u; }
+__device__ __forceinline__ uint32_t neg_inf2(__half) { return 0xFC00FC00u; }
+__device__ __forceinline__ uint32_t pos_inf2(__half) { return 0x7C007C00u; }
+
 // x / b rounded to nearest, without a division per element: with
 // y = RN(1 / b), q0 = RN(x y) is within one ulp of x / b, the residual
 // r = x - b q0 is exact in one FMA, and RN(q0 + r y) = RN(x / b)
@@ -175,13 +205,17 @@ __global__ void __launch_bounds__(kQuantThreads, POOL ? 3 : 2)
     const bool pool = POOL && job.feats != nullptr && tile < p.n_video;
     const int valid =
         POOL && p.valid != nullptr ? __ldg(p.valid + tile) : kTile;
+    // max and min run on the packed 16-bit words (widening is exact and
+    // keeps the order), sums in fp32
     float s[8], mx[8], mn[8];
+    uint32_t mxw[4], mnw[4];
     if (POOL) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        s[e] = 0.0f;
-        mx[e] = -INFINITY;
-        mn[e] = INFINITY;
+      for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        mxw[w] = neg_inf2(T());
+        mnw[w] = pos_inf2(T());
       }
     }
     float a[2] = {0.0f, 0.0f};
@@ -191,10 +225,13 @@ __global__ void __launch_bounds__(kQuantThreads, POOL ? 3 : 2)
       unpack8(raw[hh][i], f, T());
       if (POOL && pool && rg + 16 * i < valid) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          s[e] += f[e];
-          mx[e] = fmaxf(mx[e], f[e]);
-          mn[e] = fminf(mn[e], f[e]);
+        for (int e = 0; e < 8; ++e) s[e] += f[e];
+        const uint32_t w[4] = {raw[hh][i].x, raw[hh][i].y, raw[hh][i].z,
+                               raw[hh][i].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          mxw[q] = max2(mxw[q], w[q], T());
+          mnw[q] = min2(mnw[q], w[q], T());
         }
       }
 #pragma unroll
@@ -202,6 +239,8 @@ __global__ void __launch_bounds__(kQuantThreads, POOL ? 3 : 2)
         a[i >> 2] = fmaxf(a[i >> 2], fabsf(__fmul_rn(f[e], pre)));
     }
     if (POOL && pool) {
+      unpack8(make_uint4(mxw[0], mxw[1], mxw[2], mxw[3]), mx, T());
+      unpack8(make_uint4(mnw[0], mnw[1], mnw[2], mnw[3]), mn, T());
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         s[e] += __shfl_xor_sync(0xffffffffu, s[e], 16);
