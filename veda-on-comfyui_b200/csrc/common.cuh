@@ -127,35 +127,6 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, void* dst,
       : "memory");
 }
 
-// Asynchronous bulk tensor store of a shared-memory box to global memory,
-// tracked by this thread's bulk groups; the source may be rewritten once
-// bulk_wait_read() returns (the global write completes later).
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map,
-                                             const void* src, int x, int y,
-                                             int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, "
-      "%4}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
-      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-__device__ __forceinline__ void bulk_commit() {
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-// Waits until at most N of this thread's bulk groups still have their
-// shared-memory source to read.
-template <int N = 0>
-__device__ __forceinline__ void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void bulk_wait() {
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-}
-// Orders this thread's completed async-proxy (TMA) global writes before its
-// later generic-proxy accesses, so a release that follows publishes them.
-__device__ __forceinline__ void fence_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA) reads of them.
 __device__ __forceinline__ void fence_async_shared() {
