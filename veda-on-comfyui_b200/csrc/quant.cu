@@ -96,6 +96,19 @@ __device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b, __half) {
   asm("min.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+// Packed pair whose magnitudes are max(|a|, |b|) element-wise (the sign
+// bits come out as the xor of the inputs' and are cleared by the reader).
+__device__ __forceinline__ uint32_t absmax2(uint32_t a, uint32_t b,
+                                            __nv_bfloat16) {
+  uint32_t d;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t absmax2(uint32_t a, uint32_t b, __half) {
+  uint32_t d;
+  asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 __device__ __forceinline__ uint32_t neg_inf2(__nv_bfloat16) { return 0xFF80FF80u; }
 __device__ __forceinline__ uint32_t pos_inf2(__nv_bfloat16) { return 0x7F807F80u; }
 __device__ __forceinline__ uint32_t neg_inf2(__half) { return 0xFC00FC00u; }
@@ -218,25 +231,49 @@ __global__ void __launch_bounds__(kQuantThreads, POOL ? 3 : 2)
         mnw[w] = pos_inf2(T());
       }
     }
+    // max |x * pre| of rows 0-63 (a[0]) and 64-127 (a[1]). With pooling,
+    // where the SM is the limit: rounding is monotone and symmetric, so it
+    // is RN(|pre| * max |x|), and max |x| is taken on the packed 16-bit
+    // words (same bits). Without pooling the widened values are used.
     float a[2] = {0.0f, 0.0f};
+    uint32_t am[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      float f[8];
-      unpack8(raw[hh][i], f, T());
-      if (POOL && pool && rg + 16 * i < valid) {
+      const uint32_t w[4] = {raw[hh][i].x, raw[hh][i].y, raw[hh][i].z,
+                             raw[hh][i].w};
+      if (POOL) {
+        if (pool && rg + 16 * i < valid) {
+          float f[8];
+          unpack8(raw[hh][i], f, T());
 #pragma unroll
-        for (int e = 0; e < 8; ++e) s[e] += f[e];
-        const uint32_t w[4] = {raw[hh][i].x, raw[hh][i].y, raw[hh][i].z,
-                               raw[hh][i].w};
+          for (int e = 0; e < 8; ++e) s[e] += f[e];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          mxw[q] = max2(mxw[q], w[q], T());
-          mnw[q] = min2(mnw[q], w[q], T());
+          for (int q = 0; q < 4; ++q) {
+            mxw[q] = max2(mxw[q], w[q], T());
+            mnw[q] = min2(mnw[q], w[q], T());
+          }
         }
-      }
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        a[i >> 2] = fmaxf(a[i >> 2], fabsf(__fmul_rn(f[e], pre)));
+        for (int q = 0; q < 4; ++q)
+          am[i >> 2][q] = absmax2(am[i >> 2][q], w[q], T());
+      } else {
+        float f[8];
+        unpack8(raw[hh][i], f, T());
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          a[i >> 2] = fmaxf(a[i >> 2], fabsf(__fmul_rn(f[e], pre)));
+      }
+    }
+    if (POOL) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t m2 =
+            absmax2(absmax2(am[h][0], am[h][1], T()),
+                    absmax2(am[h][2], am[h][3], T()), T()) & 0x7FFF7FFFu;
+        float mf[8];
+        unpack8(make_uint4(m2, 0, 0, 0), mf, T());
+        a[h] = __fmul_rn(fmaxf(mf[0], mf[1]), fabsf(pre));
+      }
     }
     if (POOL && pool) {
       unpack8(make_uint4(mxw[0], mxw[1], mxw[2], mxw[3]), mx, T());
