@@ -125,9 +125,9 @@ TRAFFIC_SOURCE = ('ncu --set full capture of one cfg1 launch of '
 
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons, polled through NVML
-    every millisecond on a host thread while the timed region runs, so a
-    timed region of a few tens of milliseconds still gets samples. Reads
-    only; nothing is set."""
+    back to back on a host thread while the timed region runs, so a timed
+    region of ten milliseconds still gets samples. Reads only; nothing is
+    set."""
 
     # NVML clock-event reason bits (nvml.h nvmlClocksEventReason*)
     REASONS = {'sw_power_cap': 0x4, 'hw_slowdown': 0x8,
@@ -151,7 +151,8 @@ class ClockSampler:
             except Exception as error:  # noqa: BLE001 - reported
                 self.error = str(error)
                 return
-            time.sleep(0.001)
+            # back to back: a multi-GPU timed region can be ~10 ms long
+            time.sleep(0)
 
     def __enter__(self):
         import threading
@@ -198,7 +199,7 @@ class ClockSampler:
             or sm
         out = {'sm_mhz': statistics.median(loaded) if loaded else None,
                'sm_max_mhz': self.max_mhz, 'samples': len(sm),
-               'reasons': sorted(reasons), 'source': 'NVML, 1 ms polling'}
+               'reasons': sorted(reasons), 'source': 'NVML, polled back to back'}
         if self.error:
             out['error'] = self.error[:200]
         return out
