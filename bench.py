@@ -125,7 +125,7 @@ TRAFFIC_SOURCE = ('ncu --set full capture of one cfg1 launch of '
 
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons, polled through NVML
-    back to back on a host thread while the timed region runs, so a timed
+    every ~0.2 ms on a host thread while the timed region runs, so a timed
     region of ten milliseconds still gets samples. Reads only; nothing is
     set."""
 
@@ -151,8 +151,9 @@ class ClockSampler:
             except Exception as error:  # noqa: BLE001 - reported
                 self.error = str(error)
                 return
-            # back to back: a multi-GPU timed region can be ~10 ms long
-            time.sleep(0)
+            # a multi-GPU timed region can be ~10 ms long; the short pause
+            # leaves the launching thread the interpreter between polls
+            time.sleep(0.0002)
 
     def __enter__(self):
         import threading
@@ -199,7 +200,7 @@ class ClockSampler:
             or sm
         out = {'sm_mhz': statistics.median(loaded) if loaded else None,
                'sm_max_mhz': self.max_mhz, 'samples': len(sm),
-               'reasons': sorted(reasons), 'source': 'NVML, polled back to back'}
+               'reasons': sorted(reasons), 'source': 'NVML, polled every ~0.2 ms'}
         if self.error:
             out['error'] = self.error[:200]
         return out
