@@ -32,19 +32,20 @@ def _layouts(device):
         SEQ, device) for shape in SHAPES]
 
 
-def _inputs(device, layouts):
+def _inputs(device, layouts, dtype=torch.bfloat16):
     g = torch.Generator().manual_seed(31)
-    q, k, v = (torch.randn(SEQ, 6, 128, generator=g).to(torch.bfloat16)
+    q, k, v = (torch.randn(SEQ, 6, 128, generator=g).to(dtype)
                .to(device) for _ in range(3))
     scores = [torch.rand(3, lay.n_video_tiles, lay.n_video_tiles,
                          generator=g).to(device) for lay in layouts]
     return q, k, v, scores
 
 
-def test_two_shape_layer_equals_per_group_calls(cuda_device):
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
+def test_two_shape_layer_equals_per_group_calls(cuda_device, dtype):
     from veda_b200 import engine, ops, selection
     layouts = _layouts(cuda_device)
-    q, k, v, scores = _inputs(cuda_device, layouts)
+    q, k, v, scores = _inputs(cuda_device, layouts, dtype)
     budget = selection.Budget(ratio=0.3)
     attn = engine.VedaAttention(budget)
     groups = [engine.HeadGroup(lay, heads, scores=s)
