@@ -4,7 +4,7 @@
 // Arithmetic of kernels/sage/sparse_int8.py:57-73 (reference): x * pre_scale
 // in fp32; scale = max|x| / 127 per (block, head), 1 for an all-zero block;
 // q = x / scale; q += 0.5 * sign (>= 0 counts as positive); int8 = trunc(q).
-// The quotient is the IEEE-rounded one (see quant_one), so the int8 codes
+// The quotient is the IEEE-rounded one (see quant8), so the int8 codes
 // are bit-exact with an fp32 restatement of those steps.
 //
 // Pooling follows core/predictor.py:20-60: mean (fp32 sum / max(valid, 1)),
@@ -114,30 +114,56 @@ __device__ __forceinline__ uint32_t pos_inf2(__nv_bfloat16) { return 0x7F807F80u
 __device__ __forceinline__ uint32_t neg_inf2(__half) { return 0xFC00FC00u; }
 __device__ __forceinline__ uint32_t pos_inf2(__half) { return 0x7C007C00u; }
 
-// x / b rounded to nearest, without a division per element: with
-// y = RN(1 / b), q0 = RN(x y) is within one ulp of x / b, the residual
-// r = x - b q0 is exact in one FMA, and RN(q0 + r y) = RN(x / b)
-// (Markstein's theorem on FMA-corrected division). Only quotients of tiny
-// magnitude (subnormal residuals) can differ, and those quantise to 0
-// either way; the codes are those of an IEEE division.
-__device__ __forceinline__ int8_t quant_one(float x, float b, float y) {
-  const float q0 = __fmul_rn(x, y);
-  const float r = __fmaf_rn(-q0, b, x);
-  float q = __fmaf_rn(r, y, q0);
-  q = __fadd_rn(q, q >= 0.0f ? 0.5f : -0.5f);
-  return static_cast<int8_t>(__float2int_rz(q));
+// The codes of eight values f: x = RN(f pre), then x / b rounded to
+// nearest without a division per element: with y = RN(1 / b), q0 = RN(x y)
+// is within one ulp of x / b, the residual r = x - b q0 is exact in one
+// FMA, and RN(q0 + r y) = RN(x / b) (Markstein's theorem on FMA-corrected
+// division). Only quotients of tiny magnitude (subnormal residuals) can
+// differ, and those quantise to 0 either way; the codes are those of an
+// IEEE division. Then q += 0.5 with q's sign and truncation (-0 takes
+// -0.5 where the reference adds +0.5: both truncate to 0). The fp32 steps
+// run two elements at a time; each lane of a packed operation rounds as
+// its scalar form.
+__device__ __forceinline__ void quant8(const float* f, float pre, float b,
+                                       float y, int* c) {
+  const uint64_t p2 = f2(pre, pre), nb2 = f2(-b, -b), y2 = f2(y, y);
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    const uint64_t x = mul2(f2(f[e], f[e + 1]), p2);
+    const uint64_t q0 = mul2(x, y2);
+    const uint64_t r = fma2(q0, nb2, x);  // x - b q0, exact
+    float q[2];
+    f2_split(fma2(r, y2, q0), q[0], q[1]);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float h = __uint_as_float((__float_as_uint(q[k]) & 0x80000000u) |
+                                      0x3F000000u);  // 0.5 with q's sign
+      c[e + k] = __float2int_rz(__fadd_rn(q[k], h));
+    }
+  }
 }
 
-// The tile is held as raw 16-bit words (32 registers a thread) and widened
-// twice, once for the block max and once for the codes. POOL adds the
-// TripPool features; their accumulators leave room for few CTAs, so the
-// pooling variant reads its tile a second time for the codes (an L2 hit:
-// the tile was read microseconds earlier by the same CTA) and keeps three
-// CTAs per SM. Without pooling a CTA takes HEADS heads of one tile: their
-// loads are all issued before any arithmetic (16 row loads in flight per
-// thread), and a packed tile's permutation rows are read once for them.
+// The low bytes of four int32 codes, packed in order.
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  uint32_t lo, hi, r;
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(lo) : "r"(a), "r"(b));
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(hi) : "r"(c), "r"(d));
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+
+// The tile is held as raw 16-bit words (32 registers a thread); the block
+// max is taken on them and they are widened once, for the codes. POOL adds
+// the TripPool features; their accumulators leave room for few CTAs, so
+// the pooling variant reads its tile a second time for the codes (an L2
+// hit: the tile was read microseconds earlier by the same CTA) and keeps
+// three CTAs per SM. Without pooling a CTA takes HEADS heads of one tile,
+// their loads all issued before any arithmetic: one head at four CTAs per
+// SM for rows in tile order, two heads (16 row loads in flight per thread)
+// for packed rows, whose permutation rows are then read once for both.
 template <typename T, bool POOL, int HEADS>
-__global__ void __launch_bounds__(kQuantThreads, POOL ? 3 : 2)
+__global__ void __launch_bounds__(kQuantThreads,
+                                  POOL ? 3 : (HEADS == 1 ? 4 : 2))
     quant_pool_kernel(const QuantParams p) {
   __shared__ float amax_sh[8][2];
   __shared__ float pool_sh[POOL ? 8 : 1][3][kDim];
@@ -231,11 +257,10 @@ __global__ void __launch_bounds__(kQuantThreads, POOL ? 3 : 2)
         mnw[w] = pos_inf2(T());
       }
     }
-    // max |x * pre| of rows 0-63 (a[0]) and 64-127 (a[1]). With pooling,
-    // where the SM is the limit: rounding is monotone and symmetric, so it
-    // is RN(|pre| * max |x|), and max |x| is taken on the packed 16-bit
-    // words (same bits). Without pooling the widened values are used.
-    float a[2] = {0.0f, 0.0f};
+    // max |x * pre| of rows 0-63 (a[0]) and 64-127 (a[1]): rounding is
+    // monotone and symmetric, so it is RN(|pre| * max |x|), and max |x| is
+    // taken on the packed 16-bit words (same bits).
+    float a[2];
     uint32_t am[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -253,18 +278,12 @@ __global__ void __launch_bounds__(kQuantThreads, POOL ? 3 : 2)
             mnw[q] = min2(mnw[q], w[q], T());
           }
         }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          am[i >> 2][q] = absmax2(am[i >> 2][q], w[q], T());
-      } else {
-        float f[8];
-        unpack8(raw[hh][i], f, T());
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          a[i >> 2] = fmaxf(a[i >> 2], fabsf(__fmul_rn(f[e], pre)));
       }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        am[i >> 2][q] = absmax2(am[i >> 2][q], w[q], T());
     }
-    if (POOL) {
+    {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const uint32_t m2 =
@@ -352,16 +371,10 @@ __global__ void __launch_bounds__(kQuantThreads, POOL ? 3 : 2)
                          : make_uint4(0, 0, 0, 0);
       }
       unpack8(raw[hh][i], f, T());
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        lo |= static_cast<uint32_t>(static_cast<uint8_t>(
-                  quant_one(__fmul_rn(f[e], pre), b, y))) << (8 * e);
-        hi |= static_cast<uint32_t>(static_cast<uint8_t>(
-                  quant_one(__fmul_rn(f[e + 4], pre), b, y))) << (8 * e);
-      }
-      *reinterpret_cast<uint2*>(out + (rg + 16 * i) * kDim) =
-          make_uint2(lo, hi);
+      int c[8];
+      quant8(f, pre, b, y, c);
+      *reinterpret_cast<uint2*>(out + (rg + 16 * i) * kDim) = make_uint2(
+          pack4(c[0], c[1], c[2], c[3]), pack4(c[4], c[5], c[6], c[7]));
     }
     if (tid == 0) {
       if (job.block == kTile) {
@@ -380,20 +393,27 @@ int launch_quant(QuantParams p, int n_jobs, int heads, int dtype,
                  cudaStream_t stream) {
   p.n_heads = heads;
   const bool pool = p.job[0].feats != nullptr && p.n_video > 0;
-  // two heads per CTA without pooling, one with it
-  const dim3 grid(p.n_tiles, pool ? heads : (heads + 1) / 2, n_jobs);
+  // two heads per CTA for packed rows without pooling, one otherwise
+  const bool two = !pool && p.perm != nullptr;
+  const dim3 grid(p.n_tiles, two ? (heads + 1) / 2 : heads, n_jobs);
   if (dtype == VEDA_BF16) {
     if (pool)
       quant_pool_kernel<__nv_bfloat16, true, 1>
           <<<grid, kQuantThreads, 0, stream>>>(p);
-    else
+    else if (two)
       quant_pool_kernel<__nv_bfloat16, false, 2>
+          <<<grid, kQuantThreads, 0, stream>>>(p);
+    else
+      quant_pool_kernel<__nv_bfloat16, false, 1>
           <<<grid, kQuantThreads, 0, stream>>>(p);
   } else {
     if (pool)
       quant_pool_kernel<__half, true, 1><<<grid, kQuantThreads, 0, stream>>>(p);
-    else
+    else if (two)
       quant_pool_kernel<__half, false, 2>
+          <<<grid, kQuantThreads, 0, stream>>>(p);
+    else
+      quant_pool_kernel<__half, false, 1>
           <<<grid, kQuantThreads, 0, stream>>>(p);
   }
   VEDA_CHECK_CUDA(cudaGetLastError());
