@@ -94,6 +94,8 @@ int veda_quant_pool(const void* q, const void* k, int dtype, int64_t stride_n,
  *   feats_q      [heads][n_q][384] fp32; feats_k [heads][n_k][384] fp32.
  *   proj_q/k     [heads][384][128] (proj_dtype: VEDA_BF16/F16/F32).
  *   workspace    fp32 scratch of (n_q + n_k) * heads * 128 elements.
+ *   Features, projections and workspace start 16-byte aligned
+ *   (VEDA_ERR_INVALID otherwise).
  *   logits       [heads][n_q][n_k] fp32.
  */
 int veda_tile_logits(const float* feats_q, const float* feats_k,

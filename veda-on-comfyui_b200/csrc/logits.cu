@@ -13,8 +13,10 @@ namespace veda {
 namespace {
 
 constexpr int kFeat = 3 * kDim;   // 384
-constexpr int kProjRows = 16;     // rows of F per CTA in the projection
-constexpr int kLogitTile = 32;    // 32 x 32 logits per CTA
+constexpr int kProjRows = 32;     // rows of F per CTA in the projection
+constexpr int kProjChunk = 32;    // features of P per shared-memory pass
+constexpr int kLogitTile = 64;    // 64 x 64 logits per CTA
+constexpr int kLogitChunk = 32;   // dims of q_hat / k_hat per shared-memory pass
 
 template <typename PT>
 __device__ __forceinline__ float to_f(PT v);
@@ -47,14 +49,20 @@ __device__ __forceinline__ float weight<__nv_fp8_e4m3>(__nv_fp8_e4m3 v,
   return __bfloat162float(__float2bfloat16_rn(to_f(v) * scale));
 }
 
-// grid (ceil(n / 16), heads, 2): z = 0 projects q features, z = 1 k.
+// grid (ceil(n / 32), heads, 2): z = 0 projects q features, z = 1 k.
 // sq / sk: per-head scales of fp8 projections (unused otherwise).
+// A CTA takes 32 rows of F and all 128 outputs; thread (warp w, lane l)
+// accumulates rows 4 w .. 4 w + 3 x columns 4 l .. 4 l + 3, one FMA per
+// feature in ascending order (one rounding per step, as a sequential fp32
+// sum). F (transposed, feature-major) and the weights (widened to fp32)
+// pass through shared memory 32 features at a time.
 template <typename PT>
 __global__ void __launch_bounds__(256)
     project_kernel(const float* fq, const float* fk, const PT* pq,
                    const PT* pk, const float* sq, const float* sk, int n_q,
                    int n_k, float* hat_q, float* hat_k) {
-  __shared__ float f_sh[kProjRows][kFeat];
+  __shared__ __align__(16) float f_t[kProjChunk][kProjRows];  // [feature][row]
+  __shared__ __align__(16) float w_sh[kProjChunk][kDim];
   const bool is_k = blockIdx.z == 1;
   const int n = is_k ? n_k : n_q;
   const int head = blockIdx.y;
@@ -66,58 +74,154 @@ __global__ void __launch_bounds__(256)
   const float scale = scales != nullptr ? scales[head] : 1.0f;
   float* out = (is_k ? hat_k : hat_q) + (static_cast<int64_t>(head) * n + row0) * kDim;
   const int rows = min(kProjRows, n - row0);
-  for (int i = threadIdx.x; i < kProjRows * kFeat; i += blockDim.x) {
-    const int r = i / kFeat;
-    f_sh[r][i % kFeat] = r < rows ? f[i] : 0.0f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float acc[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
+  // Each thread stages 4 features of one row of F and 16 consecutive
+  // weights per chunk; the next chunk's loads are issued before this
+  // chunk's FMAs.
+  constexpr int kWords = 16 * sizeof(PT) / 16;  // 16-byte loads of weights
+  const int wi = 16 * threadIdx.x;              // first weight of the thread
+  auto load_f = [&](int k0) {
+    return lane < rows ? *reinterpret_cast<const float4*>(f + lane * kFeat +
+                                                          k0 + 4 * warp)
+                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  };
+  auto load_w = [&](int k0, uint4* raw) {
+    const uint4* src = reinterpret_cast<const uint4*>(
+        proj + static_cast<int64_t>(k0) * kDim + wi);
+#pragma unroll
+    for (int q = 0; q < kWords; ++q) raw[q] = src[q];
+  };
+  float4 fnext = load_f(0);
+  uint4 wnext[kWords];
+  load_w(0, wnext);
+  for (int k0 = 0; k0 < kFeat; k0 += kProjChunk) {
+    __syncthreads();  // the last chunk is read
+    // F transposed: lane = row, so a warp's shared stores are consecutive
+    // words
+    f_t[4 * warp][lane] = fnext.x;
+    f_t[4 * warp + 1][lane] = fnext.y;
+    f_t[4 * warp + 2][lane] = fnext.z;
+    f_t[4 * warp + 3][lane] = fnext.w;
+    {
+      const PT* wv = reinterpret_cast<const PT*>(wnext);
+      float* dst = &w_sh[0][0] + wi;
+#pragma unroll
+      for (int e = 0; e < 16; e += 4)
+        *reinterpret_cast<float4*>(dst + e) =
+            make_float4(weight(wv[e], scale), weight(wv[e + 1], scale),
+                        weight(wv[e + 2], scale), weight(wv[e + 3], scale));
+    }
+    if (k0 + kProjChunk < kFeat) {
+      fnext = load_f(k0 + kProjChunk);
+      load_w(k0 + kProjChunk, wnext);
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < kProjChunk; ++k) {
+      const float4 fv = *reinterpret_cast<const float4*>(&f_t[k][4 * warp]);
+      const float4 wv = *reinterpret_cast<const float4*>(&w_sh[k][4 * lane]);
+      const float fr[4] = {fv.x, fv.y, fv.z, fv.w};
+      const float wc[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(fr[r], wc[c], acc[r][c]);
+    }
   }
-  __syncthreads();
-  const int d = threadIdx.x & (kDim - 1);
-  const int r0 = (threadIdx.x >> 7) * (kProjRows / 2);
-  float acc[kProjRows / 2];
 #pragma unroll
-  for (int r = 0; r < kProjRows / 2; ++r) acc[r] = 0.0f;
-  for (int k = 0; k < kFeat; ++k) {
-    const float w = weight(proj[static_cast<int64_t>(k) * kDim + d], scale);
-#pragma unroll
-    for (int r = 0; r < kProjRows / 2; ++r)
-      acc[r] = fmaf(f_sh[r0 + r][k], w, acc[r]);
+  for (int r = 0; r < 4; ++r) {
+    const int row = 4 * warp + r;
+    if (row < rows) {
+      // + F[:, :128]
+      const float4 x =
+          *reinterpret_cast<const float4*>(f + row * kFeat + 4 * lane);
+      float4 o;
+      o.x = acc[r][0] + x.x;
+      o.y = acc[r][1] + x.y;
+      o.z = acc[r][2] + x.z;
+      o.w = acc[r][3] + x.w;
+      *reinterpret_cast<float4*>(out + row * kDim + 4 * lane) = o;
+    }
   }
-#pragma unroll
-  for (int r = 0; r < kProjRows / 2; ++r)
-    if (r0 + r < rows) out[(r0 + r) * kDim + d] = acc[r] + f_sh[r0 + r][d];
 }
 
-// grid (ceil(n_k / 32), ceil(n_q / 32), heads), 256 threads, 4 logits each.
+// grid (ceil(n_k / 64), ceil(n_q / 64), heads), 256 threads. A CTA takes
+// 64 x 64 logits of one head; thread (ti = t / 16, tj = t % 16) sums
+// rows 4 ti .. 4 ti + 3 x columns 4 tj .. 4 tj + 3 over the 128 dims in
+// ascending order (one fused rounding per step), with q_hat and k_hat
+// staged transposed (dim-major) 32 dims at a time.
 __global__ void __launch_bounds__(256)
     logits_kernel(const float* hat_q, const float* hat_k, int n_q, int n_k,
                   float* logits) {
-  __shared__ float q_sh[kLogitTile][kDim + 1];
-  __shared__ float k_sh[kLogitTile][kDim + 1];
+  __shared__ __align__(16) float q_t[kLogitChunk][kLogitTile];
+  __shared__ __align__(16) float k_t[kLogitChunk][kLogitTile];
   const int head = blockIdx.z;
   const int i0 = blockIdx.y * kLogitTile, j0 = blockIdx.x * kLogitTile;
   const float* qh = hat_q + static_cast<int64_t>(head) * n_q * kDim;
   const float* kh = hat_k + static_cast<int64_t>(head) * n_k * kDim;
-  for (int e = threadIdx.x; e < kLogitTile * kDim; e += blockDim.x) {
-    const int r = e / kDim, c = e % kDim;
-    q_sh[r][c] = i0 + r < n_q ? qh[static_cast<int64_t>(i0 + r) * kDim + c] : 0.0f;
-    k_sh[r][c] = j0 + r < n_k ? kh[static_cast<int64_t>(j0 + r) * kDim + c] : 0.0f;
-  }
-  __syncthreads();
-  const int tj = threadIdx.x & 31;
-  const int ti = (threadIdx.x >> 5) * 4;
-  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  for (int c = 0; c < kDim; ++c) {
-    const float kv = k_sh[tj][c];
+  const int t = threadIdx.x;
+  const int ti = t >> 4, tj = t & 15;
+  // staging: thread t moves dims 4 (t / 64) .. + 3 of row t % 64 (q and k),
+  // twice per chunk (dims +16)
+  const int sr = t & 63, sd = 4 * (t >> 6);
+  float acc[4][4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) acc[r] = fmaf(q_sh[ti + r][c], kv, acc[r]);
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
+  for (int c0 = 0; c0 < kDim; c0 += kLogitChunk) {
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int d = c0 + sd + 16 * h;
+      const float4 qv =
+          i0 + sr < n_q ? *reinterpret_cast<const float4*>(
+                              qh + static_cast<int64_t>(i0 + sr) * kDim + d)
+                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      const float4 kv =
+          j0 + sr < n_k ? *reinterpret_cast<const float4*>(
+                              kh + static_cast<int64_t>(j0 + sr) * kDim + d)
+                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      const int dd = sd + 16 * h;
+      q_t[dd][sr] = qv.x;
+      q_t[dd + 1][sr] = qv.y;
+      q_t[dd + 2][sr] = qv.z;
+      q_t[dd + 3][sr] = qv.w;
+      k_t[dd][sr] = kv.x;
+      k_t[dd + 1][sr] = kv.y;
+      k_t[dd + 2][sr] = kv.z;
+      k_t[dd + 3][sr] = kv.w;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int c = 0; c < kLogitChunk; ++c) {
+      const float4 qv = *reinterpret_cast<const float4*>(&q_t[c][4 * ti]);
+      const float4 kv = *reinterpret_cast<const float4*>(&k_t[c][4 * tj]);
+      const float qr[4] = {qv.x, qv.y, qv.z, qv.w};
+      const float kc[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          acc[r][cc] = fmaf(qr[r], kc[cc], acc[r][cc]);
+    }
   }
   const float root = 11.313708498984761f;  // sqrt(128)
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
-    const int i = i0 + ti + r, j = j0 + tj;
-    if (i < n_q && j < n_k)
-      logits[(static_cast<int64_t>(head) * n_q + i) * n_k + j] =
-          __fdiv_rn(acc[r], root);
+    const int i = i0 + 4 * ti + r;
+    if (i >= n_q) continue;
+    float* dst = logits + (static_cast<int64_t>(head) * n_q + i) * n_k;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const int j = j0 + 4 * tj + cc;
+      if (j < n_k) dst[j] = __fdiv_rn(acc[r][cc], root);
+    }
   }
 }
 
@@ -150,6 +254,11 @@ int check_logits_args(const float* feats_q, const float* feats_k,
   if (feats_q == nullptr || feats_k == nullptr || proj_q == nullptr ||
       proj_k == nullptr || logits == nullptr)
     return fail(VEDA_ERR_INVALID, "null pointer argument");
+  // the kernels read features and weights as 16-byte vectors
+  if (!aligned16(feats_q) || !aligned16(feats_k) || !aligned16(proj_q) ||
+      !aligned16(proj_k))
+    return fail(VEDA_ERR_INVALID,
+                "features and projections must be 16-byte aligned");
   return VEDA_OK;
 }
 
@@ -216,6 +325,8 @@ extern "C" int veda_tile_logits(const float* feats_q, const float* feats_k,
                                  n_k, logits))
     return rc;
   if (workspace == nullptr) return fail(VEDA_ERR_INVALID, "null workspace");
+  if (!aligned16(workspace))
+    return fail(VEDA_ERR_INVALID, "workspace must be 16-byte aligned");
   if (proj_dtype == VEDA_FP8_E4M3)
     return fail(VEDA_ERR_INVALID,
                 "fp8 projections go through veda_tile_logits_scaled");
@@ -236,6 +347,8 @@ extern "C" int veda_tile_logits_scaled(const float* feats_q,
                                  n_k, logits))
     return rc;
   if (workspace == nullptr) return fail(VEDA_ERR_INVALID, "null workspace");
+  if (!aligned16(workspace))
+    return fail(VEDA_ERR_INVALID, "workspace must be 16-byte aligned");
   return launch_tile_logits(feats_q, feats_k, proj_q, proj_k, proj_dtype,
                             scale_q, scale_k, heads, n_q, n_k, workspace,
                             logits, static_cast<cudaStream_t>(stream));
