@@ -91,6 +91,35 @@ def test_pool_and_logits_match_reference_fixture(cuda_device):
                                    rtol=1e-4, atol=1e-5)
 
 
+def test_logits_inputs_must_start_16_byte_aligned(cuda_device):
+    """The logits kernels read features and weights as 16-byte vectors: the
+    C entry point rejects a feature pointer one float past an aligned one
+    before launching anything, and the Python wrapper copies such a view
+    and gives the same logits as the aligned input."""
+    import ctypes
+    from veda_b200 import _lib, ops
+    heads, n = 2, 40
+    g = torch.Generator().manual_seed(9)
+    buf = torch.randn(heads * n * 384 + 1, generator=g).to(cuda_device)
+    fq = buf[1:].view(heads, n, 384)           # starts 4 bytes past 256
+    fk = torch.randn(heads, n, 384, generator=g).to(cuda_device)
+    pq, pk = (torch.randn(heads, 384, 128, generator=g).mul(0.05)
+              .to(torch.bfloat16).to(cuda_device) for _ in range(2))
+    assert fq.is_contiguous() and fq.data_ptr() % 16 != 0
+    lib = _lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    ws = torch.empty(2 * heads * n * 128, device=cuda_device)
+    logits = torch.full((heads, n, n), float('nan'), device=cuda_device)
+    rc = lib.veda_tile_logits(fq.data_ptr(), fk.data_ptr(), pq.data_ptr(),
+                              pk.data_ptr(), _lib.BF16, heads, n, n,
+                              ws.data_ptr(), logits.data_ptr(), stream)
+    assert rc == _lib.ERR_INVALID
+    assert b'16-byte aligned' in lib.veda_last_error()
+    assert torch.isnan(logits).all()            # nothing was written
+    want = ops.tile_logits(fq.clone(), fk, pq, pk)
+    assert torch.equal(ops.tile_logits(fq, fk, pq, pk), want)
+
+
 def test_fp8_projections_equal_the_dequantised_bf16_path(cuda_device):
     """fp8 bundle storage: the logits from fp8 weights with per-head scales
     equal, bit for bit, those from the weights the reference's loader makes

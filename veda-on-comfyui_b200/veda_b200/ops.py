@@ -209,6 +209,12 @@ def quant_pool(q: torch.Tensor, k: torch.Tensor, valid_count: torch.Tensor,
     return out
 
 
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    """`t`, or a copy of it that starts 16-byte aligned (a contiguous view
+    can start at any element; the logits kernels read 16-byte vectors)."""
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def tile_logits(feats_q: torch.Tensor, feats_k: torch.Tensor,
                 proj_q: torch.Tensor, proj_k: torch.Tensor,
                 workspace: torch.Tensor | None = None,
@@ -225,11 +231,11 @@ def tile_logits(feats_q: torch.Tensor, feats_k: torch.Tensor,
     device = require_device(feats_q, feats_k, proj_q, proj_k)
     heads, n_q, _ = feats_q.shape
     n_k = feats_k.shape[1]
-    feats_q = feats_q.float().contiguous()
-    feats_k = feats_k.float().contiguous()
+    feats_q = _aligned(feats_q.float().contiguous())
+    feats_k = _aligned(feats_k.float().contiguous())
     if proj_q.dtype != proj_k.dtype:
         raise ValueError('proj_q and proj_k must share a dtype')
-    proj_q, proj_k = proj_q.contiguous(), proj_k.contiguous()
+    proj_q, proj_k = _aligned(proj_q.contiguous()), _aligned(proj_k.contiguous())
     fp8 = proj_q.dtype == torch.float8_e4m3fn
     if fp8:
         if scale_q is None or scale_k is None:
@@ -241,7 +247,8 @@ def tile_logits(feats_q: torch.Tensor, feats_k: torch.Tensor,
         dtype = _DTYPES[proj_q.dtype]
         scale_q = scale_k = None
     need = (n_q + n_k) * heads * HEAD_DIM
-    if workspace is None or workspace.numel() < need:
+    if workspace is None or workspace.numel() < need or \
+            workspace.data_ptr() % 16:
         workspace = torch.empty(need, dtype=torch.float32, device=device)
     logits = out if out is not None else torch.empty(
         heads, n_q, n_k, dtype=torch.float32, device=device)
